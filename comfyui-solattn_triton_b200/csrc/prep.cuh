@@ -1,0 +1,71 @@
+// Parameter blocks and host launchers of the preprocessing kernels (prep.cu).
+#pragma once
+
+#include "common.cuh"
+
+namespace solb200 {
+
+struct PoolParams {
+  const __nv_bfloat16* q; const __nv_bfloat16* k; const __nv_bfloat16* v;
+  int64_t sq_b, sq_t, sq_h, sk_b, sk_t, sk_h, sv_b, sv_t, sv_h;   // element strides
+  __nv_bfloat16* kc; __nv_bfloat16* vc;      // [B, Npad, H, D]
+  float* centroid;                            // [B, N, H, D]
+  float* vamax;                               // [B, N, H, D] or null
+  int8_t* qi;                                 // [B, T, H, D] or null
+  float* qs;                                  // [B, H, tp] or null
+  int B, T, H, N, npad, blk, tp;              // tp = N * blk (row stride of qs)
+};
+
+struct MomentsParams {
+  __nv_bfloat16* kc;          // [B, Npad, H, D]; centred in place in INT8 mode
+  const float* centroid;      // [B, N, H, D]
+  const float* vamax;         // [B, N, H, D] (INT8 mode)
+  float* kmean;               // [B, H, D]
+  float* kvar;                // [B, H, D]
+  float* vscale;              // [B, H, D] (INT8 mode)
+  float* thr;                 // [B, N, H]
+  int B, H, N, npad;
+  float s2, tau;
+};
+
+struct RouteParams {
+  const __nv_bfloat16* kc;   // [B, Npad, H, D]
+  const float* centroid;     // [B, N, H, D]
+  const float* thr;          // [B, N, H]
+  uint32_t* mask;            // [B, H, N, NW]
+  int* count;                // [B, H, N]
+  int* lists;                // [B, H, N, N] or null
+  float* stat;               // [B, H, N, N] or null: (c . kc_j) * s2
+  int B, H, N, npad, nw;
+  float s2;
+  int sink_kv0, sink_kv1, sink_q0, sink_q1;
+};
+
+struct QuantParams {
+  const __nv_bfloat16* k; const __nv_bfloat16* v;
+  int64_t sk_b, sk_t, sk_h, sv_b, sv_t, sv_h;
+  const float* kmean;    // [B, H, D]
+  const float* vscale;   // [B, H, D] or null
+  int8_t* ki; float* ks; // [B, T, H, D], [B, H, tp]
+  int8_t* vi;            // [B, T, H, D] or null
+  int B, T, H, tp;       // tp = N * blk (row stride of ks)
+};
+
+struct GatherParams {
+  const char* src[4];
+  char* dst[4];
+  int ntensors;
+  int64_t src_stride_b, src_stride_row, dst_stride_b, dst_stride_row;   // bytes
+  const int64_t* index;
+  int64_t batch, rows, row_bytes;
+};
+
+void launch_pool(const PoolParams& p, int hd, bool vamax, bool qquant, cudaStream_t st);
+void launch_moments(const MomentsParams& p, int hd, bool int8, cudaStream_t st);
+void launch_route(const RouteParams& p, int hd, cudaStream_t st);
+void launch_quant_kv(const QuantParams& p, int hd, cudaStream_t st);
+void launch_morton(int64_t frames, int64_t height, int64_t width, int curve, int64_t roll,
+                   int64_t* perm, int64_t* inverse, cudaStream_t st);
+void launch_gather(const GatherParams& p, cudaStream_t st);
+
+}  // namespace solb200

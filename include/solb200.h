@@ -1,0 +1,141 @@
+/*
+ * solb200: B200-native (sm_100a) Sol-Attn block-sparse attention, C ABI.
+ *
+ * Plain pointers, sizes and a CUDA stream; no framework types. Every entry point
+ * returns an int status (SOLB200_OK = 0) and never allocates device memory: the
+ * caller passes a workspace of solb200_workspace_bytes() bytes. All launches go on
+ * the given stream, asynchronously; nothing synchronises except
+ * solb200_read_device_error(). The text of the last failure on the calling thread
+ * is available from solb200_last_error().
+ *
+ * Tensors are BTHD: [batch, tokens, heads, head_dim] with head_dim contiguous and
+ * element strides {batch, token, head} given by the caller (strides must be
+ * multiples of 8 elements and pointers 16-byte aligned). Outputs are dense BTHD.
+ *
+ * Reference interfaces these entry points replace (kijai/ComfyUI-SolAttn_triton):
+ *   solb200_sol_attn_bf16   sol_attn          _tri_fwd.py:354-434 (with prepare,
+ *                                             _preprocess.py:268-280)
+ *   solb200_sol_attn_int8   sol_attn_int8     _int8_fwd.py:379-458 (with
+ *                                             fused_preprocess, _fused_prep.py:62-98,
+ *                                             quantize_bthd / quantize_v_per_channel,
+ *                                             _fused_quant.py:45-58, 91-113)
+ *   solb200_morton_perm     morton_perm       _morton.py:35-73 and the block-aligned
+ *                                             roll of _perm_for, _morton_h3.py:42-61
+ *   solb200_gather_rows     x.index_select(1, perm) of the Morton hooks,
+ *                                             _morton.py:128,148, _morton_h3.py:192-217
+ */
+#ifndef SOLB200_H
+#define SOLB200_H
+
+#include <stdint.h>
+
+#if defined(_WIN32)
+#define SOLB200_API __declspec(dllexport)
+#else
+#define SOLB200_API __attribute__((visibility("default")))
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+enum solb200_status {
+  SOLB200_OK = 0,
+  SOLB200_ERR_INVALID = 1,    /* unsupported shape, dtype, block or argument */
+  SOLB200_ERR_ALIGNMENT = 2,  /* pointer or stride not 16-byte aligned */
+  SOLB200_ERR_WORKSPACE = 3,  /* workspace missing or too small */
+  SOLB200_ERR_CUDA = 4,       /* a CUDA runtime / driver call failed */
+  SOLB200_ERR_DEVICE = 5,     /* current device is not sm_100 */
+  SOLB200_ERR_TIMEOUT = 6     /* a device-side bounded wait gave up (see below) */
+};
+
+/* Stage selection for the attention entry points. */
+enum solb200_stages {
+  SOLB200_STAGES_ALL = 0,     /* preprocess, route, forward */
+  SOLB200_STAGES_PREPARE = 1  /* preprocess and route only (no output written) */
+};
+
+/* Workspace intermediates whose byte offsets solb200_workspace_offset() reports. */
+enum solb200_buffer {
+  SOLB200_BUF_ERROR = 0,      /* int32 device error word */
+  SOLB200_BUF_KC = 1,         /* bf16 [B, Npad, H, D] pooled keys (INT8: centred) */
+  SOLB200_BUF_VC = 2,         /* bf16 [B, Npad, H, D] pooled values (block sums) */
+  SOLB200_BUF_CENTROID = 3,   /* fp32 [B, N, H, D] query-block means */
+  SOLB200_BUF_KMEAN = 4,      /* fp32 [B, H, D] kc mean (INT8: k_mean) */
+  SOLB200_BUF_KVAR = 5,       /* fp32 [B, H, D] kc variance */
+  SOLB200_BUF_THR = 6,        /* fp32 [B, N, H] routing thresholds */
+  SOLB200_BUF_MASK = 7,       /* uint32 [B, H, N, ceil(N/32)] exact-block bits */
+  SOLB200_BUF_COUNT = 8,      /* int32 [B, H, N] exact blocks per query block */
+  SOLB200_BUF_VAMAX = 9,      /* fp32 [B, N, H, D] per-block |V| max (INT8) */
+  SOLB200_BUF_VSCALE = 10,    /* fp32 [B, H, D] V scales (INT8) */
+  SOLB200_BUF_QI = 11,        /* int8 [B, T, H, D] (INT8) */
+  SOLB200_BUF_QS = 12,        /* fp32 [B, H, N*block] (INT8; entries >= T unused) */
+  SOLB200_BUF_KI = 13,        /* int8 [B, T, H, D] (INT8) */
+  SOLB200_BUF_KS = 14,        /* fp32 [B, H, N*block] (INT8; entries >= T unused) */
+  SOLB200_BUF_VI = 15         /* int8 [B, T, H, D] (INT8) */
+};
+
+/* Thread-local text of the last failure (empty string if none). */
+SOLB200_API const char* solb200_last_error(void);
+
+/* ABI version of this library (bumped on any signature change). */
+SOLB200_API int32_t solb200_abi_version(void);
+
+/* Bytes of workspace for one call with this geometry. block: 64 or 128; head_dim:
+ * 64 or 128; int8: 0 for the BF16 path, 1 for the INT8 path. */
+SOLB200_API int32_t solb200_workspace_bytes(int64_t batch, int64_t tokens, int64_t heads, int64_t head_dim,
+                                int32_t block, int32_t int8, int64_t* bytes);
+
+/* Byte offset of an intermediate (enum solb200_buffer) inside that workspace. */
+SOLB200_API int32_t solb200_workspace_offset(int64_t batch, int64_t tokens, int64_t heads, int64_t head_dim,
+                                 int32_t block, int32_t int8, int32_t which, int64_t* offset);
+
+/* BF16 Sol-Attn. q/k/v: bf16 BTHD with strides {batch, token, head} (elements);
+ * out: dense bf16 [B, T, H, D]. scale: softmax scale (pass head_dim^-0.5 for the
+ * reference default). tau: routing threshold multiplier. sink_kv / sink_q:
+ * half-open block ranges [2] (pass {0, 0} for none). lists (nullable): int32
+ * [B, H, N, N] receives each query block's exact KV blocks in ascending order,
+ * padded with -1. route_stat (nullable): fp32 [B, H, N, N] routing scores. */
+SOLB200_API int32_t solb200_sol_attn_bf16(const void* q, const int64_t* q_strides, const void* k,
+                              const int64_t* k_strides, const void* v, const int64_t* v_strides,
+                              void* out, int64_t batch, int64_t tokens, int64_t heads,
+                              int64_t head_dim, int32_t block, float scale, float tau,
+                              const int64_t* sink_kv, const int64_t* sink_q, int32_t stages,
+                              void* workspace, int64_t workspace_bytes, int32_t* lists,
+                              float* route_stat, void* stream);
+
+/* INT8 Sol-Attn (per-token int8 Q and K with K smoothed by the pooled-key mean; with
+ * int8_pv, per-channel int8 V and per-row int8 P). Same arguments as the BF16 entry
+ * point plus int8_pv (1 = INT8 P*V, 0 = BF16 P*V). */
+SOLB200_API int32_t solb200_sol_attn_int8(const void* q, const int64_t* q_strides, const void* k,
+                              const int64_t* k_strides, const void* v, const int64_t* v_strides,
+                              void* out, int64_t batch, int64_t tokens, int64_t heads,
+                              int64_t head_dim, int32_t block, float scale, float tau,
+                              const int64_t* sink_kv, const int64_t* sink_q, int32_t int8_pv,
+                              int32_t stages, void* workspace, int64_t workspace_bytes,
+                              int32_t* lists, float* route_stat, void* stream);
+
+/* Synchronise `stream`, read the workspace's device error word into *code and clear
+ * it. Returns SOLB200_ERR_TIMEOUT when a kernel recorded a bounded-wait timeout. */
+SOLB200_API int32_t solb200_read_device_error(void* workspace, int32_t* code, void* stream);
+
+/* Morton (Z-order) permutation of a (frames, height, width) token grid in row-major
+ * order: perm[i] = token at position i, inverse[token] = position. curve: 0 = "3d",
+ * 1 = "2d_frame". roll: rotation of the permutation (the H3 block alignment uses
+ * (-span_start) mod block); 0 for the plain permutation. perm/inverse: int64 device
+ * arrays of frames*height*width entries. */
+SOLB200_API int32_t solb200_morton_perm(int64_t frames, int64_t height, int64_t width, int32_t curve,
+                            int64_t roll, int64_t* perm, int64_t* inverse, void* stream);
+
+/* dst[b, i, :] = src[b, index[i], :] for up to 4 tensors that share one geometry:
+ * rows of row_bytes (a multiple of 16) with byte strides {batch, row}. */
+SOLB200_API int32_t solb200_gather_rows(const void* const* src, void* const* dst, int32_t ntensors,
+                            const int64_t* index, int64_t batch, int64_t rows, int64_t row_bytes,
+                            int64_t src_stride_b, int64_t src_stride_row, int64_t dst_stride_b,
+                            int64_t dst_stride_row, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* SOLB200_H */

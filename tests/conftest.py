@@ -36,3 +36,9 @@ def cuda_device():
     if major != 10:
         pytest.skip("kernels are built for sm_100a only")
     return torch.device("cuda:0")
+
+
+# GPU tests read each call's device error word (bounded-wait timeouts surface as
+# RuntimeError instead of silently wrong output).
+import os as _os
+_os.environ.setdefault("SOLB200_SYNC_CHECK", "1")
