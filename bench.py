@@ -107,6 +107,9 @@ def run_ours(args, rank, world, local_rank):
     from solb200.workloads import CONFIGS, make_qkv
 
     cfg = CONFIGS["c3"]
+    if args.heads:
+        import dataclasses
+        cfg = dataclasses.replace(cfg, heads=args.heads)
     dev = torch.device("cuda", local_rank)
     torch.cuda.set_device(dev)
     B, T, Hall, D, blk = cfg.batch, cfg.tokens, cfg.heads, cfg.head_dim, cfg.block
@@ -195,10 +198,11 @@ def run_ours(args, rank, world, local_rank):
         o = fn(dq, dk, dv, tau=cfg.tau, block=blk)
         hout.copy_(o, non_blocking=True)
 
-    for _ in range(2):
-        e2e_step()
-    e2e_steps = max(2, min(args.steps, 5))
-    ms_e2e = timed(e2e_step, e2e_steps)
+    ms_e2e = None
+    if not args.no_e2e:
+        for _ in range(2):
+            e2e_step()
+        ms_e2e = timed(e2e_step, max(2, min(args.steps, 5)))
     h2d = sum(t.numel() * t.element_size() for t in (hq, hk, hv))
     d2h = hout.numel() * hout.element_size()
 
@@ -234,7 +238,7 @@ def run_ours(args, rank, world, local_rank):
         "vs_baseline": None,
         "dtype": "int8" if int8 else "bf16",
         "data": "synthetic (seeded smooth+noise video-DiT q/k/v, solb200.workloads)",
-        "config": {"workload": "config3_video480p_B1_H40_T32760_D128_blk128_tau0.9",
+        "config": {"workload": "config3_video480p_B1_H%d_T32760_D128_blk128_tau0.9" % cfg.heads,
                    "path": args.path, "heads_per_rank": H, "parallelism": f"heads/{world}",
                    "l2": "inputs larger than L2 (3 x 335 MB)", "routed_density": density},
         "stages_ms": {"prep_route": ms_prep, "forward": ms_fwd, "reorder_qkv_and_o": ms_reorder},
@@ -245,8 +249,9 @@ def run_ours(args, rank, world, local_rank):
                      "frac": achieved / peaks["bf16"], "traffic": None,
                      "note": f"executed flops {fwd_flops:.4g} per launch / forward time; "
                              f"peak = bf16 dense burst, {peaks['source']}"},
-        "e2e": {"value": dense_job / (ms_e2e * 1e-3) / 1e12, "unit": UNIT, "ms_per_step": ms_e2e,
-                "h2d_bytes_per_step": h2d * world, "d2h_bytes_per_step": d2h * world},
+        "e2e": ({"value": dense_job / (ms_e2e * 1e-3) / 1e12, "unit": UNIT, "ms_per_step": ms_e2e,
+                 "h2d_bytes_per_step": h2d * world, "d2h_bytes_per_step": d2h * world}
+                if ms_e2e else None),
         "gpu_launches": 4 * args.steps + (1 if int8 else 0) * args.steps,
         "clocks": clocks,
     }
@@ -322,6 +327,9 @@ def main():
     ap.add_argument("--no-dense", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-units", type=int, default=64)
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--heads", type=int, default=0,
+                    help="profiling only: run this many of the 40 heads (0 = all)")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
 
