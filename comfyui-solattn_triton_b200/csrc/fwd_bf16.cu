@@ -161,66 +161,20 @@ sol_fwd_bf16_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_const
       if (!(ok = mbar_wait_warp(bar_sfull, t & 1, p.err, kErrWaitSoftmax))) break;
       tc_fence_after();
       uint32_t colmask[4];
-      float w_tail = 0.f;
-      int tail_col = -1;
       if (kind == kTileApprox) {
-        it.approx_bits(idx, colmask);
         // column of the last (ragged) block, weighed by its true length
-        if (p.N - 1 >= idx * 128 && p.N - 1 < idx * 128 + 128) {
-          tail_col = p.N - 1 - idx * 128;
-          w_tail = (float)(p.T - (p.N - 1) * BLK);
-        }
-      } else {
+        it.approx_bits(idx, colmask);
+        const int tail_col = (p.N - 1 >= idx * 128 && p.N - 1 < idx * 128 + 128) ? p.N - 1 - idx * 128 : -1;
+        softmax_tile<128, true, true, HD>(tS + lane_base, tO + lane_base, colmask, p.s2, m_ref, l_sum, t > 0,
+                                          tail_col, (float)(p.T - (p.N - 1) * BLK), (float)BLK);
+      } else if ((idx + 1) * BLK > p.T) {
         token_bits<BLK>(p.T - idx * BLK, colmask);
+        softmax_tile<BLK, true, false, HD>(tS + lane_base, tO + lane_base, colmask, p.s2, m_ref, l_sum, t > 0,
+                                           -1, 0.f, 1.f);
+      } else {
+        softmax_tile<BLK, false, false, HD>(tS + lane_base, tO + lane_base, colmask, p.s2, m_ref, l_sum,
+                                            t > 0, -1, 0.f, 1.f);
       }
-      const int nchunks = (kind == kTileApprox ? 128 : BLK) / 32;
-      const float w_full = kind == kTileApprox ? (float)BLK : 1.f;
-      // pass 1: masked row max of the raw scores (scaling by s2 > 0 is monotone)
-      float mx = -INFINITY;
-      for (int c = 0; c < nchunks; ++c) {
-        uint32_t r[32];
-        tmem_ld32(tS + lane_base + c * 32, r);
-        tmem_wait_ld();
-#pragma unroll
-        for (int i = 0; i < 32; ++i)
-          if ((colmask[c] >> i) & 1u) mx = fmaxf(mx, __uint_as_float(r[i]));
-      }
-      mx = mx * p.s2;
-      const float m_new = fmaxf(m_ref, mx);
-      float alpha = 1.f;
-      bool need = false;
-      if (m_ref == -INFINITY) {
-        m_ref = m_new;
-      } else if (m_new > m_ref + 8.f) {
-        alpha = fast_exp2(m_ref - m_new);
-        m_ref = m_new;
-        need = true;
-      }
-      if (__any_sync(0xffffffffu, need) && t > 0) {
-        l_sum *= alpha;
-        rescale_rows<HD>(tO + lane_base, alpha);
-      }
-      const float m_use = m_ref == -INFINITY ? 0.f : m_ref;
-      // pass 2: probabilities, row sum, bf16 P into the consumed score columns
-      float lsum = 0.f;
-      for (int c = 0; c < nchunks; ++c) {
-        uint32_t r[32];
-        tmem_ld32(tS + lane_base + c * 32, r);
-        tmem_wait_ld();
-        uint32_t pk[16];
-#pragma unroll
-        for (int i = 0; i < 32; i += 2) {
-          const bool v0 = (colmask[c] >> i) & 1u, v1 = (colmask[c] >> (i + 1)) & 1u;
-          const float p0 = v0 ? fast_exp2(fmaf(__uint_as_float(r[i]), p.s2, -m_use)) : 0.f;
-          const float p1 = v1 ? fast_exp2(fmaf(__uint_as_float(r[i + 1]), p.s2, -m_use)) : 0.f;
-          const int col = c * 32 + i;
-          lsum += p0 * (col == tail_col ? w_tail : w_full);
-          lsum += p1 * (col + 1 == tail_col ? w_tail : w_full);
-          pk[i >> 1] = pack_bf16x2(p0, p1);
-        }
-        tmem_st16(tS + lane_base + c * 16, pk);
-      }
-      l_sum += lsum;
       tmem_wait_st();
       tc_fence_before();
       mbar_arrive(bar_pfull);

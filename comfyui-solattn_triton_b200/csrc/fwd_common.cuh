@@ -109,6 +109,12 @@ __device__ __forceinline__ float fast_exp2(float x) {
   return y;
 }
 
+__device__ __forceinline__ float max3(float a, float b, float c) {
+  float r;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));
+  return r;
+}
+
 // Multiply this warp's 32 TMEM lanes of an HD-column fp32 accumulator by a per-row
 // factor (every thread passes its own row's factor).
 template <int HD>
@@ -122,6 +128,69 @@ __device__ __forceinline__ void rescale_rows(uint32_t taddr, float f) {
     for (int i = 0; i < 32; ++i) r[i] = __float_as_uint(__uint_as_float(r[i]) * f);
     tmem_st32(taddr + c * 32, r);
   }
+}
+
+// One tile of the online softmax for this thread's row (= TMEM lane), NCOLS score
+// columns in TMEM at `t_s` (fp32). MASKED: columns whose bit in `colmask` is clear
+// are excluded. WEIGHTED: the row sum weighs every column by `w_full`, except column
+// `tail_col` by `w_tail` (pooled blocks stand for their token count).
+// Updates the reference max m_ref (raised only when the tile exceeds it by more than
+// 2^8; then this warp's accumulator rows in TMEM at `t_o` are rescaled when o_live)
+// and the row sum l_sum, and writes bf16 P over the first NCOLS/2 score columns.
+template <int NCOLS, bool MASKED, bool WEIGHTED, int HD>
+__device__ __forceinline__ void softmax_tile(uint32_t t_s, uint32_t t_o, const uint32_t (&colmask)[4],
+                                             float s2, float& m_ref, float& l_sum, bool o_live,
+                                             int tail_col, float w_tail, float w_full) {
+  uint32_t r[NCOLS];
+#pragma unroll
+  for (int c = 0; c < NCOLS / 32; ++c) tmem_ld32(t_s + c * 32, *reinterpret_cast<uint32_t(*)[32]>(&r[c * 32]));
+  tmem_wait_ld();
+  if (MASKED) {
+#pragma unroll
+    for (int i = 0; i < NCOLS; ++i)
+      if (!((colmask[i >> 5] >> (i & 31)) & 1u)) r[i] = __float_as_uint(-INFINITY);
+  }
+  float m4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+#pragma unroll
+  for (int i = 0; i < NCOLS; i += 8) {
+    m4[(i >> 3) & 3] = max3(m4[(i >> 3) & 3], max3(__uint_as_float(r[i]), __uint_as_float(r[i + 1]),
+                                                   __uint_as_float(r[i + 2])),
+                            max3(__uint_as_float(r[i + 3]), __uint_as_float(r[i + 4]),
+                                 fmaxf(__uint_as_float(r[i + 5]),
+                                       fmaxf(__uint_as_float(r[i + 6]), __uint_as_float(r[i + 7])))));
+  }
+  const float mx = max3(m4[0], m4[1], fmaxf(m4[2], m4[3])) * s2;
+  const float m_new = fmaxf(m_ref, mx);
+  float alpha = 1.f;
+  bool need = false;
+  if (m_ref == -INFINITY) {
+    m_ref = m_new;
+  } else if (m_new > m_ref + 8.f) {
+    alpha = fast_exp2(m_ref - m_new);
+    m_ref = m_new;
+    need = true;
+  }
+  if (__any_sync(0xffffffffu, need) && o_live) {
+    l_sum *= alpha;
+    rescale_rows<HD>(t_o, alpha);
+  }
+  const float neg_m = m_ref == -INFINITY ? 0.f : -m_ref;
+  float acc[4] = {0.f, 0.f, 0.f, 0.f};
+  float tail_p = 0.f;
+#pragma unroll
+  for (int i = 0; i < NCOLS; i += 2) {
+    const float p0 = fast_exp2(fmaf(__uint_as_float(r[i]), s2, neg_m));
+    const float p1 = fast_exp2(fmaf(__uint_as_float(r[i + 1]), s2, neg_m));
+    acc[(i >> 1) & 3] += p0 + p1;
+    if (WEIGHTED) tail_p += (i == tail_col ? p0 : 0.f) + (i + 1 == tail_col ? p1 : 0.f);
+    r[i >> 1] = pack_bf16x2(p0, p1);   // P overwrites already-consumed registers
+  }
+  float s = (acc[0] + acc[1]) + (acc[2] + acc[3]);
+  if (WEIGHTED) s = s * w_full + tail_p * (w_tail - w_full);
+  l_sum += s;
+#pragma unroll
+  for (int c = 0; c < NCOLS / 32; ++c)
+    tmem_st16(t_s + c * 16, *reinterpret_cast<const uint32_t(*)[16]>(&r[c * 16]));
 }
 
 cudaError_t launch_fwd_bf16(int hd, int blk, const FwdMaps& m, const FwdParams& p, cudaStream_t st);
