@@ -256,15 +256,20 @@ int32_t run(const Plan& P, const Call& c) {
   FwdMaps m;
   const int64_t npad = P.npad;
   if ((rc = make_map(&m.q, c.q, false, P.D, P.H, P.T, P.B, c.sq[2], c.sq[1], c.sq[0], 128, "q"))) return rc;
-  if ((rc = make_map(&m.kc, pp.kc, false, P.D, P.H, npad, P.B, P.D, P.H * P.D, npad * P.H * P.D, 128, "kc")))
+  // the BF16 kernel streams 64-row halves; the INT8 kernel 128-row pooled chunks
+  const int pooled_rows = c.int8 ? 128 : 64;
+  const int kv_rows = c.int8 ? P.blk : 64;
+  if ((rc = make_map(&m.kc, pp.kc, false, P.D, P.H, npad, P.B, P.D, P.H * P.D, npad * P.H * P.D, pooled_rows,
+                     "kc")))
     return rc;
-  if ((rc = make_map(&m.vc, pp.vc, false, P.D, P.H, npad, P.B, P.D, P.H * P.D, npad * P.H * P.D, 128, "vc")))
+  if ((rc = make_map(&m.vc, pp.vc, false, P.D, P.H, npad, P.B, P.D, P.H * P.D, npad * P.H * P.D, pooled_rows,
+                     "vc")))
     return rc;
   if ((rc = make_map(&m.o, c.out, false, P.D, P.H, P.T, P.B, P.D, P.H * P.D, P.T * P.H * P.D, P.blk, "out")))
     return rc;
   if (!c.int8) {
-    if ((rc = make_map(&m.k, c.k, false, P.D, P.H, P.T, P.B, c.sk[2], c.sk[1], c.sk[0], P.blk, "k"))) return rc;
-    if ((rc = make_map(&m.v, c.v, false, P.D, P.H, P.T, P.B, c.sv[2], c.sv[1], c.sv[0], P.blk, "v"))) return rc;
+    if ((rc = make_map(&m.k, c.k, false, P.D, P.H, P.T, P.B, c.sk[2], c.sk[1], c.sk[0], kv_rows, "k"))) return rc;
+    if ((rc = make_map(&m.v, c.v, false, P.D, P.H, P.T, P.B, c.sv[2], c.sv[1], c.sv[0], kv_rows, "v"))) return rc;
     e = launch_fwd_bf16(hd, P.blk, m, fp, c.st);
     if (e != cudaSuccess) return cuda_fail(e, "bf16 forward launch");
     return SOLB200_OK;
@@ -279,7 +284,7 @@ int32_t run(const Plan& P, const Call& c) {
                        P.T * TD, P.blk, "vi")))
       return rc;
   } else {
-    if ((rc = make_map(&m.v, c.v, false, P.D, P.H, P.T, P.B, c.sv[2], c.sv[1], c.sv[0], P.blk, "v"))) return rc;
+    if ((rc = make_map(&m.v, c.v, false, P.D, P.H, P.T, P.B, c.sv[2], c.sv[1], c.sv[0], kv_rows, "v"))) return rc;
   }
   fp.qs = pp.qs;
   fp.ks = at<float>(c.ws, P, SOLB200_BUF_KS);

@@ -95,6 +95,54 @@ struct TileIter {
   }
 };
 
+// The same walk in 64-row halves, the unit of the forward pipeline: each approximate
+// chunk contributes the halves (64 pooled rows) that hold approximate columns, each
+// routed block contributes its 64-token halves that hold at least one real token.
+// row0 is the first pooled row (approximate) or token (exact) of the half.
+template <int BLK>
+struct HalfIter {
+  TileIter tiles;
+  int T;
+  int pend0, pend1;   // the current tile's halves (scalars: no local-memory array)
+  int npend, ipend, pkind;
+
+  __device__ HalfIter(const FwdParams& p, const UnitInfo& u)
+      : tiles(p, u), T(p.T), pend0(0), pend1(0), npend(0), ipend(0), pkind(0) {}
+
+  __device__ __forceinline__ bool next(int& kind, int& row0) {
+    while (ipend >= npend) {
+      int k, idx;
+      if (!tiles.next(k, idx)) return false;
+      ipend = 0;
+      pkind = k;
+      if (k == kTileApprox) {
+        uint32_t b[4];
+        tiles.approx_bits(idx, b);
+        const bool lo = (b[0] | b[1]) != 0, hi = (b[2] | b[3]) != 0;
+        pend0 = lo ? idx * 128 : idx * 128 + 64;
+        pend1 = idx * 128 + 64;
+        npend = (lo ? 1 : 0) + (hi ? 1 : 0);
+      } else {
+        pend0 = idx * BLK;
+        pend1 = idx * BLK + 64;
+        npend = (BLK == 128 && idx * BLK + 64 < T) ? 2 : 1;
+      }
+    }
+    kind = pkind;
+    row0 = ipend == 0 ? pend0 : pend1;
+    ++ipend;
+    return true;
+  }
+
+  // approximate-column bits of the 64 pooled rows starting at row0 (a multiple of 64)
+  __device__ __forceinline__ void approx_bits64(int row0, uint32_t (&out)[2]) const {
+    uint32_t b[4];
+    tiles.approx_bits(row0 >> 7, b);
+    out[0] = (row0 & 64) ? b[2] : b[0];
+    out[1] = (row0 & 64) ? b[3] : b[1];
+  }
+};
+
 // Bits of the key columns of an exact tile that hold real tokens (valid = T - kv0).
 template <int BLK>
 __device__ __forceinline__ void token_bits(int valid, uint32_t (&out)[4]) {
@@ -191,6 +239,75 @@ __device__ __forceinline__ void softmax_tile(uint32_t t_s, uint32_t t_o, const u
 #pragma unroll
   for (int c = 0; c < NCOLS / 32; ++c)
     tmem_st16(t_s + c * 16, *reinterpret_cast<const uint32_t(*)[16]>(&r[c * 16]));
+}
+
+// One 64-column half of the online softmax for this thread's row. Same contract as
+// softmax_tile, plus `before_rescale`, called (warp-uniformly) before the accumulator
+// rows are rescaled so the caller can wait for in-flight P*V products first.
+template <bool MASKED, bool WEIGHTED, int HD, typename Hook>
+__device__ __forceinline__ void softmax_half(uint32_t t_s, uint32_t t_o, const uint32_t (&colmask)[2], float s2,
+                                             float& m_ref, float& l_sum, bool o_live, int tail_col,
+                                             float w_tail, float w_full, Hook&& before_rescale) {
+  uint32_t ra[32], rb[32];
+  tmem_ld32(t_s, ra);
+  tmem_ld32(t_s + 32, rb);
+  tmem_wait_ld();
+  if (MASKED) {
+#pragma unroll
+    for (int i = 0; i < 32; ++i) {
+      if (!((colmask[0] >> i) & 1u)) ra[i] = __float_as_uint(-INFINITY);
+      if (!((colmask[1] >> i) & 1u)) rb[i] = __float_as_uint(-INFINITY);
+    }
+  }
+  float m4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+#pragma unroll
+  for (int i = 0; i < 32; i += 4) {
+    m4[(i >> 2) & 3] = max3(m4[(i >> 2) & 3],
+                            max3(__uint_as_float(ra[i]), __uint_as_float(ra[i + 1]), __uint_as_float(ra[i + 2])),
+                            max3(__uint_as_float(ra[i + 3]), __uint_as_float(rb[i]),
+                                 max3(__uint_as_float(rb[i + 1]), __uint_as_float(rb[i + 2]),
+                                      __uint_as_float(rb[i + 3]))));
+  }
+  const float mx = max3(m4[0], m4[1], fmaxf(m4[2], m4[3])) * s2;
+  const float m_new = fmaxf(m_ref, mx);
+  float alpha = 1.f;
+  bool need = false;
+  if (m_ref == -INFINITY) {
+    m_ref = m_new;
+  } else if (m_new > m_ref + 8.f) {
+    alpha = fast_exp2(m_ref - m_new);
+    m_ref = m_new;
+    need = true;
+  }
+  if (__any_sync(0xffffffffu, need) && o_live) {
+    before_rescale();
+    l_sum *= alpha;
+    rescale_rows<HD>(t_o, alpha);
+  }
+  const float neg_m = m_ref == -INFINITY ? 0.f : -m_ref;
+  float acc[4] = {0.f, 0.f, 0.f, 0.f};
+  float tail_p = 0.f;
+  uint32_t pa[16], pb[16];
+#pragma unroll
+  for (int i = 0; i < 32; i += 2) {
+    const float p0 = fast_exp2(fmaf(__uint_as_float(ra[i]), s2, neg_m));
+    const float p1 = fast_exp2(fmaf(__uint_as_float(ra[i + 1]), s2, neg_m));
+    const float p2 = fast_exp2(fmaf(__uint_as_float(rb[i]), s2, neg_m));
+    const float p3 = fast_exp2(fmaf(__uint_as_float(rb[i + 1]), s2, neg_m));
+    acc[(i >> 1) & 1] += p0 + p1;
+    acc[2 + ((i >> 1) & 1)] += p2 + p3;
+    if (WEIGHTED) {
+      tail_p += (i == tail_col ? p0 : 0.f) + (i + 1 == tail_col ? p1 : 0.f);
+      tail_p += (i + 32 == tail_col ? p2 : 0.f) + (i + 33 == tail_col ? p3 : 0.f);
+    }
+    pa[i >> 1] = pack_bf16x2(p0, p1);
+    pb[i >> 1] = pack_bf16x2(p2, p3);
+  }
+  float s = (acc[0] + acc[1]) + (acc[2] + acc[3]);
+  if (WEIGHTED) s = s * w_full + tail_p * (w_tail - w_full);
+  l_sum += s;
+  tmem_st16(t_s, pa);
+  tmem_st16(t_s + 16, pb);
 }
 
 cudaError_t launch_fwd_bf16(int hd, int blk, const FwdMaps& m, const FwdParams& p, cudaStream_t st);
