@@ -157,6 +157,25 @@ __device__ __forceinline__ float fast_exp2(float x) {
   return y;
 }
 
+// Packed fp32 pairs (Blackwell f32x2 FMA / add): one instruction for two lanes' worth
+// of arithmetic.
+__device__ __forceinline__ float2 fma2(float2 a, float2 b, float2 c) {
+  uint64_t r;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;"
+      : "=l"(r)
+      : "l"(*reinterpret_cast<uint64_t*>(&a)), "l"(*reinterpret_cast<uint64_t*>(&b)),
+        "l"(*reinterpret_cast<uint64_t*>(&c)));
+  return *reinterpret_cast<float2*>(&r);
+}
+
+__device__ __forceinline__ float2 add2(float2 a, float2 b) {
+  uint64_t r;
+  asm("add.f32x2 %0, %1, %2;"
+      : "=l"(r)
+      : "l"(*reinterpret_cast<uint64_t*>(&a)), "l"(*reinterpret_cast<uint64_t*>(&b)));
+  return *reinterpret_cast<float2*>(&r);
+}
+
 __device__ __forceinline__ float max3(float a, float b, float c) {
   float r;
   asm("max.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));
@@ -285,25 +304,27 @@ __device__ __forceinline__ void softmax_half(uint32_t t_s, uint32_t t_o, const u
     rescale_rows<HD>(t_o, alpha);
   }
   const float neg_m = m_ref == -INFINITY ? 0.f : -m_ref;
-  float acc[4] = {0.f, 0.f, 0.f, 0.f};
+  const float2 s2v = make_float2(s2, s2), nmv = make_float2(neg_m, neg_m);
+  float2 acc[4] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
   float tail_p = 0.f;
   uint32_t pa[16], pb[16];
 #pragma unroll
   for (int i = 0; i < 32; i += 2) {
-    const float p0 = fast_exp2(fmaf(__uint_as_float(ra[i]), s2, neg_m));
-    const float p1 = fast_exp2(fmaf(__uint_as_float(ra[i + 1]), s2, neg_m));
-    const float p2 = fast_exp2(fmaf(__uint_as_float(rb[i]), s2, neg_m));
-    const float p3 = fast_exp2(fmaf(__uint_as_float(rb[i + 1]), s2, neg_m));
-    acc[(i >> 1) & 1] += p0 + p1;
-    acc[2 + ((i >> 1) & 1)] += p2 + p3;
+    const float2 xa = fma2(make_float2(__uint_as_float(ra[i]), __uint_as_float(ra[i + 1])), s2v, nmv);
+    const float2 xb = fma2(make_float2(__uint_as_float(rb[i]), __uint_as_float(rb[i + 1])), s2v, nmv);
+    const float2 pa2 = make_float2(fast_exp2(xa.x), fast_exp2(xa.y));
+    const float2 pb2 = make_float2(fast_exp2(xb.x), fast_exp2(xb.y));
+    acc[(i >> 1) & 1] = add2(acc[(i >> 1) & 1], pa2);
+    acc[2 + ((i >> 1) & 1)] = add2(acc[2 + ((i >> 1) & 1)], pb2);
     if (WEIGHTED) {
-      tail_p += (i == tail_col ? p0 : 0.f) + (i + 1 == tail_col ? p1 : 0.f);
-      tail_p += (i + 32 == tail_col ? p2 : 0.f) + (i + 33 == tail_col ? p3 : 0.f);
+      tail_p += (i == tail_col ? pa2.x : 0.f) + (i + 1 == tail_col ? pa2.y : 0.f);
+      tail_p += (i + 32 == tail_col ? pb2.x : 0.f) + (i + 33 == tail_col ? pb2.y : 0.f);
     }
-    pa[i >> 1] = pack_bf16x2(p0, p1);
-    pb[i >> 1] = pack_bf16x2(p2, p3);
+    pa[i >> 1] = pack_bf16x2(pa2.x, pa2.y);
+    pb[i >> 1] = pack_bf16x2(pb2.x, pb2.y);
   }
-  float s = (acc[0] + acc[1]) + (acc[2] + acc[3]);
+  const float2 a01 = add2(add2(acc[0], acc[1]), add2(acc[2], acc[3]));
+  float s = a01.x + a01.y;
   if (WEIGHTED) s = s * w_full + tail_p * (w_tail - w_full);
   l_sum += s;
   tmem_st16(t_s, pa);
