@@ -5,6 +5,7 @@
 #include <string>
 
 #include "fwd_common.cuh"
+#include "internal.h"
 #include "prep.cuh"
 #include "solb200.h"
 
@@ -425,3 +426,25 @@ int32_t solb200_gather_rows(const void* const* src, void* const* dst, int32_t nt
 }
 
 }  // extern "C"
+
+namespace solb200 {
+
+int32_t set_last_error(int32_t code, const std::string& msg) { return fail(code, msg); }
+
+int32_t set_cuda_error(cudaError_t e, const char* what) { return cuda_fail(e, what); }
+
+int32_t plan_workspace_bytes(int64_t B, int64_t T, int64_t H, int64_t D, int32_t block, int32_t int8,
+                             int64_t* bytes) {
+  return solb200_workspace_bytes(B, T, H, D, block, int8, bytes);
+}
+
+int32_t run_attention(const void* q, const int64_t* sq, const void* k, const int64_t* sk, const void* v,
+                      const int64_t* sv, void* out, int64_t B, int64_t T, int64_t H, int64_t D, int32_t blk,
+                      float scale, float tau, const int64_t* sink_kv, const int64_t* sink_q, bool int8,
+                      bool int8_pv, int32_t stages, void* ws, int64_t ws_bytes, int32_t* lists, float* stat,
+                      void* stream) {
+  return attn_entry(q, sq, k, sk, v, sv, out, B, T, H, D, blk, scale, tau, sink_kv, sink_q, int8, int8_pv,
+                    stages, ws, ws_bytes, lists, stat, stream);
+}
+
+}  // namespace solb200

@@ -44,6 +44,10 @@ _SIGS = {
                                         POINTER(c_int64), c_void_p, c_int64, c_int64, c_int64, c_int64,
                                         c_int32, c_float, c_float, POINTER(c_int64), POINTER(c_int64),
                                         c_int32, c_int32, c_void_p, c_int64, c_void_p, c_void_p, c_void_p]),
+    "solb200_sol_attn_bf16_noalloc": (c_int32, [c_void_p, POINTER(c_int64), c_void_p, POINTER(c_int64),
+                                                c_void_p, POINTER(c_int64), c_void_p, c_int64, c_int64,
+                                                c_int64, c_int64, c_int32, c_float, c_float,
+                                                POINTER(c_int64), POINTER(c_int64), c_void_p]),
     "solb200_read_device_error": (c_int32, [c_void_p, POINTER(c_int32), c_void_p]),
     "solb200_morton_perm": (c_int32, [c_int64, c_int64, c_int64, c_int32, c_int64, c_void_p, c_void_p,
                                       c_void_p]),

@@ -115,6 +115,26 @@ SOLB200_API int32_t solb200_sol_attn_int8(const void* q, const int64_t* q_stride
                               int32_t stages, void* workspace, int64_t workspace_bytes,
                               int32_t* lists, float* route_stat, void* stream);
 
+/* BF16 Sol-Attn that allocates nothing, for hosts that cannot hand this library device
+ * memory at call time (an application that plans all device allocations up front and
+ * forbids allocating later, a plugin whose host owns the allocator, or a caller that
+ * cannot afford cudaMalloc's implicit synchronisation in the attention path).
+ * No counterpart in the reference. Same arguments and result as
+ * solb200_sol_attn_bf16 without stages, workspace, lists and route_stat: the scratch
+ * is a fixed 16 MiB __device__ array inside this library (held on every GPU that loads
+ * the library, until exit). The 40-head, 32760-token, head_dim-128 call needs 10.9 MB
+ * at 128-token blocks and fits; at 64-token blocks it needs 22.5 MB and, like any call
+ * whose solb200_workspace_bytes exceeds 16 MiB, returns SOLB200_ERR_WORKSPACE. The first call on a device looks up the array's address on
+ * that device; make it before any stream capture. All calls on a device share the
+ * array: calls that overlap on the GPU race and must be serialised by the caller. */
+SOLB200_API int32_t solb200_sol_attn_bf16_noalloc(const void* q, const int64_t* q_strides, const void* k,
+                                                  const int64_t* k_strides, const void* v,
+                                                  const int64_t* v_strides, void* out, int64_t batch,
+                                                  int64_t tokens, int64_t heads, int64_t head_dim,
+                                                  int32_t block, float scale, float tau,
+                                                  const int64_t* sink_kv, const int64_t* sink_q,
+                                                  void* stream);
+
 /* Synchronise `stream`, read the workspace's device error word into *code and clear
  * it. Returns SOLB200_ERR_TIMEOUT when a kernel recorded a bounded-wait timeout. */
 SOLB200_API int32_t solb200_read_device_error(void* workspace, int32_t* code, void* stream);
