@@ -44,6 +44,20 @@ def load_peaks():
     return dict(hbm=6650.0, bf16=1590.0, bf16_sus=1400.0, source="fallback")
 
 
+def profiled_traffic(path, heads):
+    """DRAM bytes (read + write) of one forward launch at `heads` heads, from the ncu
+    capture summarised in profiles/sol_fwd_<path>_config3.md (a line
+    `traffic_bytes_per_head: N`; every head's work is independent, so traffic scales
+    with the head count). None when there is no capture for this path."""
+    f = REPO / "profiles" / f"sol_fwd_{path}_config3.md"
+    if not f.exists():
+        return None
+    for line in f.read_text().splitlines():
+        if line.strip().startswith("traffic_bytes_per_head:"):
+            return float(line.split(":", 1)[1].strip().strip("`")) * heads
+    return None
+
+
 class Clocks:
     """nvidia-smi sampling during the timed region."""
 
@@ -104,6 +118,7 @@ def run_ours(args, rank, world, local_rank):
     import solb200
     from solb200 import _lib
     from solb200.ops import STAGES_ALL, STAGES_PREPARE, I64x2, I64x3, Workspace
+    from solb200._lib import STAGES_FORWARD
     from solb200.workloads import CONFIGS, make_qkv
 
     cfg = CONFIGS["c3"]
@@ -161,11 +176,16 @@ def run_ours(args, rank, world, local_rank):
         ms = timed(lambda: call(STAGES_ALL), args.steps)
     ws.check_device_error()
     clocks = clk.result
-    # stage split (same stream, same inputs): preprocess + routing alone
+    # stage split (same stream, same inputs): preprocess + routing alone, then the
+    # forward kernel alone over the workspace the last call left (CUDA events on the
+    # stream the kernels are launched on)
     for _ in range(2):
         call(STAGES_PREPARE)
     ms_prep = timed(lambda: call(STAGES_PREPARE), args.steps)
-    ms_fwd = max(ms - ms_prep, 1e-6)
+    for _ in range(2):
+        call(STAGES_FORWARD)
+    ms_fwd = timed(lambda: call(STAGES_FORWARD), args.steps)
+    ws.check_device_error()
 
     # executed (algorithmic) flops of the forward from the routing of this input
     counts = ws.view("count", torch.int32, (B, H, ws.N)).long()
@@ -246,9 +266,11 @@ def run_ours(args, rank, world, local_rank):
         "sparse_over_dense": (ms / ms_dense) if isinstance(ms_dense, float) else None,
         "roofline": {"bound": "tensor", "kernel": "sol_fwd_%s_kernel" % ("int8" if int8 else "bf16"),
                      "achieved": achieved, "peak": peaks["bf16"], "unit": "TFLOP/s",
-                     "frac": achieved / peaks["bf16"], "traffic": None,
-                     "note": f"executed flops {fwd_flops:.4g} per launch / forward time; "
-                             f"peak = bf16 dense burst, {peaks['source']}"},
+                     "frac": achieved / peaks["bf16"],
+                     "traffic": profiled_traffic("int8" if int8 else "bf16", H),
+                     "note": f"executed flops {fwd_flops:.4g} per launch / forward kernel time; "
+                             f"peak = bf16 dense burst, {peaks['source']}; traffic = DRAM bytes "
+                             f"per launch from the ncu capture in profiles/, scaled to {H} heads"},
         "e2e": ({"value": dense_job / (ms_e2e * 1e-3) / 1e12, "unit": UNIT, "ms_per_step": ms_e2e,
                  "h2d_bytes_per_step": h2d * world, "d2h_bytes_per_step": d2h * world}
                 if ms_e2e else None),

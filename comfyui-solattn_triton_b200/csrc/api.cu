@@ -172,9 +172,10 @@ int32_t run(const Plan& P, const Call& c) {
   if ((rc = check_tensor("q", c.q, c.sq, P.B))) return rc;
   if ((rc = check_tensor("k", c.k, c.sk, P.B))) return rc;
   if ((rc = check_tensor("v", c.v, c.sv, P.B))) return rc;
-  if (c.stages != SOLB200_STAGES_ALL && c.stages != SOLB200_STAGES_PREPARE)
+  if (c.stages != SOLB200_STAGES_ALL && c.stages != SOLB200_STAGES_PREPARE && c.stages != SOLB200_STAGES_FORWARD)
     return fail(SOLB200_ERR_INVALID, "unknown stages value");
-  if (c.stages == SOLB200_STAGES_ALL && (!c.out || !aligned16(c.out)))
+  const bool prep = c.stages != SOLB200_STAGES_FORWARD;
+  if (c.stages != SOLB200_STAGES_PREPARE && (!c.out || !aligned16(c.out)))
     return fail(SOLB200_ERR_ALIGNMENT, "out: null or not 16-byte aligned");
   if (!c.ws || c.ws_bytes < P.total)
     return fail(SOLB200_ERR_WORKSPACE, "workspace is " + std::to_string(c.ws_bytes) + " bytes, needs " +
@@ -202,7 +203,7 @@ int32_t run(const Plan& P, const Call& c) {
   pp.qs = c.int8 ? at<float>(c.ws, P, SOLB200_BUF_QS) : nullptr;
   pp.B = (int)P.B; pp.T = (int)P.T; pp.H = (int)P.H; pp.N = P.N; pp.npad = P.npad; pp.blk = P.blk;
   pp.tp = P.N * P.blk;
-  launch_pool(pp, hd, pp.vamax != nullptr, c.int8, c.st);
+  if (prep) launch_pool(pp, hd, pp.vamax != nullptr, c.int8, c.st);
 
   MomentsParams mp{};
   mp.kc = pp.kc;
@@ -214,9 +215,9 @@ int32_t run(const Plan& P, const Call& c) {
   mp.thr = at<float>(c.ws, P, SOLB200_BUF_THR);
   mp.B = (int)P.B; mp.H = (int)P.H; mp.N = P.N; mp.npad = P.npad;
   mp.s2 = s2; mp.tau = c.tau;
-  launch_moments(mp, hd, c.int8, c.st);
+  if (prep) launch_moments(mp, hd, c.int8, c.st);
 
-  if (c.int8) {
+  if (c.int8 && prep) {
     QuantParams qp{};
     qp.k = pp.k; qp.v = pp.v;
     qp.sk_b = pp.sk_b; qp.sk_t = pp.sk_t; qp.sk_h = pp.sk_h;
@@ -244,7 +245,7 @@ int32_t run(const Plan& P, const Call& c) {
   auto clampi = [&](int64_t x) { return (int)(x < -lim ? -lim : (x > lim ? lim : x)); };
   rp.sink_kv0 = clampi(c.sink_kv[0]); rp.sink_kv1 = clampi(c.sink_kv[1]);
   rp.sink_q0 = clampi(c.sink_q[0]); rp.sink_q1 = clampi(c.sink_q[1]);
-  launch_route(rp, hd, c.st);
+  if (prep) launch_route(rp, hd, c.st);
   e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, "preprocess launch");
   if (c.stages == SOLB200_STAGES_PREPARE) return SOLB200_OK;

@@ -52,7 +52,9 @@ enum solb200_status {
 /* Stage selection for the attention entry points. */
 enum solb200_stages {
   SOLB200_STAGES_ALL = 0,     /* preprocess, route, forward */
-  SOLB200_STAGES_PREPARE = 1  /* preprocess and route only (no output written) */
+  SOLB200_STAGES_PREPARE = 1, /* preprocess and route only (no output written) */
+  SOLB200_STAGES_FORWARD = 2  /* forward only, over a workspace that an earlier ALL or PREPARE
+                                 call with the same inputs and geometry filled (profiling) */
 };
 
 /* Workspace intermediates whose byte offsets solb200_workspace_offset() reports. */
