@@ -24,7 +24,8 @@ struct FwdMaps {
 
 struct UnitInfo {
   int b, h, qb;
-  const uint32_t* row;   // this unit's nw mask words
+  const uint32_t* row;   // this unit's nw mask words: global memory or a shared-memory
+                         // copy, so they are read with generic (not ld.global.nc) loads
 };
 
 // Units are numbered head-major, (b*H + h)*N + qb, so CTAs that run together share
@@ -62,7 +63,7 @@ struct TileIter {
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
       const int wi = chunk * 4 + i;
-      out[i] = wi < nw ? (~__ldg(row + wi)) & low_bits(N - wi * 32) : 0u;
+      out[i] = wi < nw ? (~row[wi]) & low_bits(N - wi * 32) : 0u;
     }
   }
 
@@ -90,7 +91,7 @@ struct TileIter {
         return true;
       }
       if (++w >= nw) return false;
-      bits = __ldg(row + w);
+      bits = row[w];
     }
   }
 };
@@ -333,6 +334,8 @@ __device__ __forceinline__ void softmax_half(uint32_t t_s, uint32_t t_o, const u
 
 cudaError_t launch_fwd_bf16(int hd, int blk, const FwdMaps& m, const FwdParams& p, cudaStream_t st);
 cudaError_t launch_fwd_int8(int hd, int blk, const FwdMaps& m, const FwdParams& p, cudaStream_t st);
+// the pipelined INT8 kernel (head_dim 128, 128-token blocks)
+cudaError_t launch_fwd_int8p(const FwdMaps& m, const FwdParams& p, cudaStream_t st);
 size_t fwd_bf16_smem_bytes(int hd);
 
 }  // namespace solb200

@@ -446,7 +446,8 @@ static cudaError_t launch_t(const FwdMaps& m, const FwdParams& p, cudaStream_t s
 }
 
 cudaError_t launch_fwd_int8(int hd, int blk, const FwdMaps& m, const FwdParams& p, cudaStream_t st) {
-  if (hd == 128 && blk == 128) return launch_t<128, 128>(m, p, st);
+  // head_dim 128 with 128-token blocks (the video shapes) runs the pipelined kernel
+  if (hd == 128 && blk == 128) return launch_fwd_int8p(m, p, st);
   if (hd == 128 && blk == 64) return launch_t<128, 64>(m, p, st);
   if (hd == 64 && blk == 128) return launch_t<64, 128>(m, p, st);
   return launch_t<64, 64>(m, p, st);

@@ -1,0 +1,552 @@
+// Pipelined INT8 Sol-Attn block-sparse forward for head_dim 128 and 128-token blocks
+// (the video shapes); other shapes use the serial kernel in fwd_int8.cu.
+//
+// Tile walk and arithmetic follow _forward_int8_ptr (_int8_fwd.py:190-372):
+//   approximate tiles (128 pooled keys): bf16 q . kc^T (kind::f16, q and kc in shared
+//     memory), bf16 P . vc accumulated into O by the tensor core; the row sum weighs
+//     each pooled column by its block length (_int8_fwd.py:288-308).
+//   exact tiles (one routed 128-token block): S = qi . ki^T on kind::i8 (int32),
+//     scores = S * (qs * s2) * ks (_int8_fwd.py:311-332).
+//     INT8 P.V (int8_pv): pe = 2^(s - blockmax), pi = int8(min(pe*127 + 0.5, 127)) in
+//       shared memory, PV = pi . vi on kind::i8 into its own TMEM columns, folded into
+//       O by the softmax warps as O = O * alpha + PV * (beta / 127) * vscale[d] with
+//       beta = 2^(blockmax - m) (_int8_fwd.py:336-353).
+//     BF16 P.V: P = 2^(s - m) in bf16 in TMEM, P . V (bf16) accumulated into O.
+//
+// One CTA per unit, one CTA per SM (all 512 TMEM columns):
+//   TMEM  [0,128) bf16 P (64 columns) or int32 P.V | [128,256) O | [256,384) S slot 0 |
+//         [384,512) S slot 1
+//   smem  q bf16 32 KB | qi 16 KB | K ring 2 x 32 KB | V ring 2 x 32 KB | int8 P 16 KB |
+//         ks ring of 4 tiles, vscale, mask row, max / sum exchange
+// Warps 0-7 softmax (warps w and w+4 share the rows of TMEM lanes 32(w%4).. and split
+// each tile's 128 columns), warp 8 TMA producer, warp 9 TMEM allocator + MMA issuer.
+// The issuer keeps the tensor core idle while the softmax loads a tile's scores (a TMEM
+// load waits behind in-flight MMAs): per tile, the softmax loads S(j+1), then P.V(j)
+// and Q.K^T(j+2) run while it works on tile j+1. The fold of an int8 P.V(j) into O is
+// done by the softmax warps when they next need the P / P.V columns (tile j+1, or the
+// epilogue). Every wait is bounded; every softmax thread runs every tile and every
+// named barrier, also after a failed wait (the work is skipped, the barriers are not).
+#include "common.cuh"
+#include "fwd_common.cuh"
+
+namespace solb200 {
+
+namespace {
+
+constexpr int kMaskCapI8 = 1024;   // routing-mask words of one unit kept in shared memory
+
+// Maximum of this thread's 64 values (fp32 bits in `r`); with MASKED, columns whose bit
+// in `cm` (2 words) is clear are set to -inf first.
+template <bool MASKED>
+__device__ __forceinline__ float max64(uint32_t (&r)[64], const uint32_t (&cm)[2]) {
+  if (MASKED) {
+#pragma unroll
+    for (int i = 0; i < 64; ++i)
+      if (!((cm[i >> 5] >> (i & 31)) & 1u)) r[i] = __float_as_uint(-INFINITY);
+  }
+  float m4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+#pragma unroll
+  for (int i = 0; i < 64; i += 8) {
+    m4[(i >> 3) & 3] = max3(m4[(i >> 3) & 3],
+                            max3(__uint_as_float(r[i]), __uint_as_float(r[i + 1]), __uint_as_float(r[i + 2])),
+                            max3(__uint_as_float(r[i + 3]), __uint_as_float(r[i + 4]),
+                                 max3(__uint_as_float(r[i + 5]), __uint_as_float(r[i + 6]),
+                                      __uint_as_float(r[i + 7]))));
+  }
+  return max3(m4[0], m4[1], fmaxf(m4[2], m4[3]));
+}
+
+// P = 2^(r * sc - m) as bf16 pairs in r[0..31] (pair k = columns 2k, 2k+1); returns the
+// row sum of the 64 columns, weighing column `tail_col` by w_tail and every other by
+// w_full when WEIGHTED.
+template <bool WEIGHTED>
+__device__ __forceinline__ float exp_bf16_64(uint32_t (&r)[64], float sc, float m, int tail_col, float w_tail,
+                                             float w_full) {
+  const float2 scv = make_float2(sc, sc), nmv = make_float2(-m, -m);
+  float2 acc[4] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
+  float tail_p = 0.f;
+#pragma unroll
+  for (int i = 0; i < 64; i += 2) {
+    const float2 x = fma2(make_float2(__uint_as_float(r[i]), __uint_as_float(r[i + 1])), scv, nmv);
+    const float2 pp = make_float2(fast_exp2(x.x), fast_exp2(x.y));
+    acc[(i >> 1) & 3] = add2(acc[(i >> 1) & 3], pp);
+    if (WEIGHTED) tail_p += (i == tail_col ? pp.x : 0.f) + (i + 1 == tail_col ? pp.y : 0.f);
+    r[i >> 1] = pack_bf16x2(pp.x, pp.y);
+  }
+  const float2 a = add2(add2(acc[0], acc[1]), add2(acc[2], acc[3]));
+  float sum = a.x + a.y;
+  if (WEIGHTED) sum = sum * w_full + tail_p * (w_tail - w_full);
+  return sum;
+}
+
+// int32 -> float without the conversion unit (which the exponentials share): for
+// |x| < 2^22 the bits 0x4B400000 + x are the float 1.5*2^23 + x, exact; removing
+// 1.5*2^23 leaves float(x) exactly. Scores qi . ki are below 128 * 127^2 < 2^22.
+__device__ __forceinline__ float i2f_exact(uint32_t x) {
+  return __uint_as_float(x + 0x4B400000u) - 12582912.f;
+}
+
+// pe = 2^(r - bm) in [0, 1] for the 64 columns (log2-unit scores in r); the int8 codes
+// min(pe*127 + 0.5, 127) truncated (_int8_fwd.py:350) packed four per word into q[16];
+// returns the sum of pe. The truncation of y in [0.5, 127] is the low byte of
+// y + 2^23 rounded toward zero (an FMA-pipe add instead of a conversion).
+__device__ __forceinline__ float exp_int8_64(const uint32_t (&r)[64], float bm, uint32_t (&q)[16]) {
+  float2 acc = make_float2(0.f, 0.f);
+#pragma unroll
+  for (int w = 0; w < 16; ++w) {
+    uint32_t b[4];
+#pragma unroll
+    for (int e = 0; e < 4; e += 2) {
+      const float2 pe = make_float2(fast_exp2(__uint_as_float(r[w * 4 + e]) - bm),
+                                    fast_exp2(__uint_as_float(r[w * 4 + e + 1]) - bm));
+      acc = add2(acc, pe);
+      b[e] = __float_as_uint(__fadd_rz(fminf(__fadd_rn(__fmul_rn(pe.x, 127.f), 0.5f), 127.f), 8388608.f));
+      b[e + 1] = __float_as_uint(__fadd_rz(fminf(__fadd_rn(__fmul_rn(pe.y, 127.f), 0.5f), 127.f), 8388608.f));
+    }
+    // low bytes of b[0], b[1] -> bytes 0, 1 of lo (likewise hi); then lo.0 lo.1 hi.0 hi.1
+    uint32_t lo, hi, word;
+    asm("prmt.b32 %0, %1, %2, 0x0040;" : "=r"(lo) : "r"(b[0]), "r"(b[1]));
+    asm("prmt.b32 %0, %1, %2, 0x0040;" : "=r"(hi) : "r"(b[2]), "r"(b[3]));
+    asm("prmt.b32 %0, %1, %2, 0x5410;" : "=r"(word) : "r"(lo), "r"(hi));
+    q[w] = word;
+  }
+  return acc.x + acc.y;
+}
+
+}  // namespace
+
+__global__ void __launch_bounds__(320, 1)
+sol_fwd_int8p_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_kc,
+                     const __grid_constant__ CUtensorMap tm_vc, const __grid_constant__ CUtensorMap tm_o,
+                     const __grid_constant__ CUtensorMap tm_qi, const __grid_constant__ CUtensorMap tm_ki,
+                     const __grid_constant__ CUtensorMap tm_vi, const __grid_constant__ CUtensorMap tm_v,
+                     const FwdParams p) {
+  constexpr int HD = 128, BLK = 128;
+  constexpr uint32_t BOX = 128 * 128;           // 128 rows x 128 bytes
+  constexpr uint32_t TILE = 2 * BOX;            // 128 rows x 128 bf16
+  constexpr int KST = 2, VST = 2;
+  constexpr uint32_t IDESC_QK_BF16 = make_idesc(kFmtF32, kFmtBF16, kFmtBF16, 0, 0, 128, 128);
+  constexpr uint32_t IDESC_PV_BF16 = make_idesc(kFmtF32, kFmtBF16, kFmtBF16, 0, 1, 128, HD);
+  constexpr uint32_t IDESC_QK_I8 = make_idesc(kFmtS32, kFmtS8, kFmtS8, 0, 0, 128, 128);
+  constexpr uint32_t IDESC_PV_I8 = make_idesc(kFmtS32, kFmtS8, kFmtS8, 0, 1, 128, HD);
+
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sQ = smem;                    // bf16 q (approximate tiles); later the O staging
+  uint8_t* sQI = sQ + TILE;              // int8 qi, 128 rows x 128 bytes
+  uint8_t* sK = sQI + BOX;               // KST stages: kc (bf16, 32 KB) or ki (int8, 16 KB)
+  uint8_t* sV = sK + KST * TILE;         // VST stages: vc / v (bf16) or vi (int8)
+  uint8_t* sP = sV + VST * TILE;         // int8 P, 128 rows x 128 bytes
+  float* sKS = reinterpret_cast<float*>(sP + BOX);   // [4][128] key scales, by tile j % 4
+  float* sVSC = sKS + 4 * 128;                       // [HD] value scales
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sVSC + HD);
+  uint64_t* bar_q = bars + 0;            // q, qi, vscale staged
+  uint64_t* bar_kfull = bars + 1;        // [KST]
+  uint64_t* bar_kfree = bars + 3;        // [KST] Q.K^T of the stage's tile complete
+  uint64_t* bar_vfull = bars + 5;        // [VST]
+  uint64_t* bar_vfree = bars + 7;        // [VST] P.V of the stage's tile complete
+  uint64_t* bar_sfree = bars + 9;        // [2] scores of a slot loaded by the softmax (256)
+  uint64_t* bar_pfull = bars + 11;       // P written, previous int8 P.V folded (256)
+  uint64_t* bar_drain = bars + 12;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 13);
+  uint32_t* sMask = reinterpret_cast<uint32_t*>(bars + 16);    // kMaskCapI8 words
+  float* sMax = reinterpret_cast<float*>(sMask + kMaskCapI8);   // [2 tiles][2 halves][128 rows]
+  float* sSum = sMax + 512;                                      // [2 halves][128 rows]
+  int* sBad = reinterpret_cast<int*>(sSum + 256);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  UnitInfo u = decode_unit(p, blockIdx.x);
+  const int bh = u.b * p.H + u.h;
+  const int tp = p.N * BLK;
+  const bool pv8 = p.int8_pv != 0;
+  if (p.nw <= kMaskCapI8)
+    for (int i = threadIdx.x; i < p.nw; i += blockDim.x) sMask[i] = __ldg(u.row + i);
+
+  if (threadIdx.x == 0) {
+    *sBad = 0;
+    mbar_init(bar_q, 1);
+    for (int i = 0; i < KST; ++i) {
+      mbar_init(bar_kfull + i, 1);
+      mbar_init(bar_kfree + i, 1);
+    }
+    for (int i = 0; i < VST; ++i) {
+      mbar_init(bar_vfull + i, 1);
+      mbar_init(bar_vfree + i, 1);
+    }
+    for (int i = 0; i < 2; ++i) mbar_init(bar_sfree + i, 256);
+    mbar_init(bar_pfull, 256);
+    mbar_init(bar_drain, 1);
+    fence_barrier_init();
+  }
+  if (warp == 9) {
+    tmem_alloc(tmem_slot, 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (p.nw <= kMaskCapI8) u.row = sMask;
+  const uint32_t tmem = *tmem_slot;
+  const uint32_t tA = tmem, tO = tmem + 128, tS = tmem + 256;
+
+  if (warp == 8) {
+    // ------------------------------------------------------------ TMA producer
+    // q, qi, vscale; K0 K1, V0 V1; then per tile j: K(j+2) once Q.K^T(j) is done with
+    // its stage (its key scales go to ring slot (j+2) % 4, which the softmax finished
+    // with at tile j-2), V(j+2) once P.V(j) is done.
+    if (lane == 0) {
+      tma_prefetch_desc(&tm_q);
+      tma_prefetch_desc(&tm_kc);
+      tma_prefetch_desc(&tm_vc);
+      tma_prefetch_desc(&tm_qi);
+      tma_prefetch_desc(&tm_ki);
+      tma_prefetch_desc(pv8 ? &tm_vi : &tm_v);
+      mbar_arrive_expect_tx(bar_q, TILE + BOX + (pv8 ? HD * 4 : 0));
+      for (int i = 0; i < 2; ++i) tma_load_4d(sQ + i * BOX, &tm_q, bar_q, i * 64, u.h, u.qb * BLK, u.b);
+      tma_load_4d(sQI, &tm_qi, bar_q, 0, u.h, u.qb * BLK, u.b);
+      if (pv8) bulk_load(sVSC, p.vscale + (int64_t)bh * HD, HD * 4, bar_q);
+      auto load_k = [&](int stage, int kind, int idx, int jt) {
+        uint64_t* bar = bar_kfull + stage;
+        uint8_t* dst = sK + stage * TILE;
+        if (kind == kTileApprox) {
+          mbar_arrive_expect_tx(bar, TILE);
+          for (int i = 0; i < 2; ++i) tma_load_4d(dst + i * BOX, &tm_kc, bar, i * 64, u.h, idx * 128, u.b);
+        } else {
+          mbar_arrive_expect_tx(bar, BOX + BLK * 4);
+          tma_load_4d(dst, &tm_ki, bar, 0, u.h, idx * BLK, u.b);
+          bulk_load(sKS + (jt & 3) * 128, p.ks + (int64_t)bh * tp + (int64_t)idx * BLK, BLK * 4, bar);
+        }
+      };
+      auto load_v = [&](int stage, int kind, int idx) {
+        uint64_t* bar = bar_vfull + stage;
+        uint8_t* dst = sV + stage * TILE;
+        if (kind == kTileApprox) {
+          mbar_arrive_expect_tx(bar, TILE);
+          for (int i = 0; i < 2; ++i) tma_load_4d(dst + i * BOX, &tm_vc, bar, i * 64, u.h, idx * 128, u.b);
+        } else if (pv8) {
+          mbar_arrive_expect_tx(bar, BOX);
+          tma_load_4d(dst, &tm_vi, bar, 0, u.h, idx * BLK, u.b);
+        } else {
+          mbar_arrive_expect_tx(bar, TILE);
+          for (int i = 0; i < 2; ++i) tma_load_4d(dst + i * BOX, &tm_v, bar, i * 64, u.h, idx * BLK, u.b);
+        }
+      };
+      TileIter itk(p, u), itv(p, u);
+      int kind, idx, nk = 0, nv = 0;
+      bool ok = true;
+      while (nk < KST && itk.next(kind, idx)) load_k(nk % KST, kind, idx, nk), ++nk;
+      while (nv < VST && itv.next(kind, idx)) load_v(nv % VST, kind, idx), ++nv;
+      for (int j = 0; ok; ++j) {
+        bool more = false;
+        if (itk.next(kind, idx)) {
+          more = true;
+          if (!(ok = mbar_wait(bar_kfree + j % KST, (j / KST) & 1, p.err, kErrWaitLoad))) break;
+          load_k(nk % KST, kind, idx, nk);
+          ++nk;
+        }
+        if (itv.next(kind, idx)) {
+          more = true;
+          if (!(ok = mbar_wait(bar_vfree + j % VST, (j / VST) & 1, p.err, kErrWaitLoad))) break;
+          load_v(nv % VST, kind, idx);
+          ++nv;
+        }
+        if (!more) break;
+      }
+      if (!ok) {
+        // exit path: the newest copy of every stage must land before shared memory goes away
+        mbar_wait(bar_q, 0, p.err, kErrWaitDrain);
+        for (int i = nk - 1; i >= 0 && i >= nk - KST; --i)
+          mbar_wait(bar_kfull + i % KST, (i / KST) & 1, p.err, kErrWaitDrain);
+        for (int i = nv - 1; i >= 0 && i >= nv - VST; --i)
+          mbar_wait(bar_vfull + i % VST, (i / VST) & 1, p.err, kErrWaitDrain);
+      }
+    }
+  } else if (warp == 9) {
+    // -------------------------------------------------------------- MMA issuer
+    if (lane == 0) {
+      // descriptors of the tile bases; a stage / K-step adds its byte offset >> 4 to
+      // the start-address field (shared addresses stay below 2^18: nothing carries)
+      const uint64_t qd = make_sw128_desc(smem_u32(sQ), 16, 1024);
+      const uint64_t qid = make_sw128_desc(smem_u32(sQI), 16, 1024);
+      const uint64_t kd0 = make_sw128_desc(smem_u32(sK), 16, 1024);
+      const uint64_t vd0 = make_sw128_desc(smem_u32(sV), BOX, 1024);   // bf16 V, MN-major
+      const uint64_t vid0 = make_sw128_desc(smem_u32(sV), 0, 1024);    // int8 V, MN-major
+      const uint64_t pd = make_sw128_desc(smem_u32(sP), 16, 1024);     // int8 P, K-major
+      auto issue_qk = [&](int j, int kind) {
+        const int st = j % KST;
+        const uint32_t d = tS + (j & 1) * 128;
+        const uint64_t kd = kd0 + (uint64_t)(st * (TILE >> 4));
+        if (kind == kTileApprox) {
+#pragma unroll
+          for (int k = 0; k < HD / 16; ++k) {
+            const uint32_t off = ((k >> 2) * BOX + (k & 3) * 32) >> 4;
+            mma_bf16_ss(d, qd + (uint64_t)off, kd + (uint64_t)off, IDESC_QK_BF16, k > 0);
+          }
+        } else {
+#pragma unroll
+          for (int k = 0; k < HD / 32; ++k)
+            mma_i8_ss(d, qid + (uint64_t)(k * 2), kd + (uint64_t)(k * 2), IDESC_QK_I8, k > 0);
+        }
+        tc_commit(bar_kfree + st);
+      };
+      bool ok = mbar_wait(bar_q, 0, p.err, kErrWaitMma);
+      tc_fence_after();
+      TileIter itq(p, u), itp(p, u);
+      int kind, idx, jq = 0;
+      while (ok && jq < 2 && itq.next(kind, idx)) {
+        if (!(ok = mbar_wait(bar_kfull + jq % KST, (jq / KST) & 1, p.err, kErrWaitMma))) break;
+        tc_fence_after();
+        issue_qk(jq++, kind);
+      }
+      for (int j = 0; ok && itp.next(kind, idx); ++j) {
+        // P.V(j) once P(j) is written and the softmax holds the scores of tile j+1,
+        // then Q.K^T(j+2) into the slot the softmax released at tile j
+        if (!(ok = mbar_wait(bar_pfull, j & 1, p.err, kErrWaitMma))) break;
+        int qkind, qidx;
+        const bool more = itq.next(qkind, qidx);   // tile j+2
+        TileIter peek = itp;
+        int k1, i1;
+        if (peek.next(k1, i1) &&
+            !(ok = mbar_wait(bar_sfree + ((j + 1) & 1), ((j + 1) >> 1) & 1, p.err, kErrWaitMma)))
+          break;
+        if (!(ok = mbar_wait(bar_vfull + j % VST, (j / VST) & 1, p.err, kErrWaitMma))) break;
+        tc_fence_after();
+        const uint32_t vo = (j % VST) * (TILE >> 4);
+        if (kind == kTileExact && pv8) {
+#pragma unroll
+          for (int kk = 0; kk < BLK / 32; ++kk)
+            mma_i8_ss(tA, pd + (uint64_t)(kk * 2), vid0 + (uint64_t)(vo + kk * (4096 >> 4)), IDESC_PV_I8, kk > 0);
+        } else {
+          const uint32_t acc0 = j > 0 ? 1u : 0u;
+#pragma unroll
+          for (int kk = 0; kk < 8; ++kk)
+            mma_bf16_ts(tO, tA + kk * 8, vd0 + (uint64_t)(vo + kk * (2048 >> 4)), IDESC_PV_BF16,
+                        kk > 0 ? 1u : acc0);
+        }
+        tc_commit(bar_vfree + j % VST);
+        if (more) {
+          if (!(ok = mbar_wait(bar_sfree + (j & 1), (j >> 1) & 1, p.err, kErrWaitMma))) break;
+          if (!(ok = mbar_wait(bar_kfull + (j + 2) % KST, ((j + 2) / KST) & 1, p.err, kErrWaitMma))) break;
+          tc_fence_after();
+          issue_qk(j + 2, qkind);
+        }
+      }
+      // every MMA this thread issued has completed once bar_drain fires
+      tc_commit(bar_drain);
+      mbar_wait(bar_drain, 0, p.err, kErrWaitDrain);
+    }
+  } else {
+    // -------------------------------- softmax, folds, epilogue (rows x column halves)
+    const int row = threadIdx.x & 127;                 // TMEM lane / query row
+    const int h = threadIdx.x >> 7;                    // column half of tiles and of O
+    const uint32_t lane_base = (uint32_t)((warp & 3) * 32) << 16;
+    const int qrow = u.qb * BLK + row;
+    const float qs_log2 = (qrow < p.T ? __ldg(p.qs + (int64_t)bh * tp + qrow) : 0.f) * p.s2;
+    bool ok = mbar_wait_warp(bar_q, 0, p.err, kErrWaitSoftmax);   // vscale is staged with q
+    float m_ref = -INFINITY, l_sum = 0.f;
+    bool o_live = false;      // O holds a contribution
+    bool fold_pending = false;
+    float f_alpha = 1.f, f_scale = 0.f;   // the pending int8 P.V fold: O*alpha + PV*scale*vscale
+    int j = 0, kind, idx;
+    // fold an int8 P.V (complete) into this thread's half of O
+    auto fold = [&]() {
+      if (!ok) return;
+#pragma unroll 1
+      for (int c = 0; c < 2; ++c) {
+        uint32_t pv[32], o[32];
+        tmem_ld32(tA + lane_base + h * 64 + c * 32, pv);
+        if (o_live) tmem_ld32(tO + lane_base + h * 64 + c * 32, o);
+        tmem_wait_ld();
+        const float4* vs4 = reinterpret_cast<const float4*>(sVSC + h * 64 + c * 32);
+#pragma unroll
+        for (int i = 0; i < 32; i += 4) {
+          const float4 v4 = vs4[i >> 2];
+          const float vv[4] = {v4.x, v4.y, v4.z, v4.w};
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            // |P.V| <= 128 * 127 * 127 < 2^22: exact through the magic-number conversion
+            const float add = i2f_exact(pv[i + e]) * (f_scale * vv[e]);
+            o[i + e] = __float_as_uint(o_live ? fmaf(__uint_as_float(o[i + e]), f_alpha, add) : add);
+          }
+        }
+        tmem_st32(tO + lane_base + h * 64 + c * 32, o);
+      }
+      tmem_wait_st();
+      o_live = true;
+    };
+    TileIter it(p, u);
+    for (; it.next(kind, idx); ++j) {
+      const bool exact = kind == kTileExact;
+      uint32_t r[64];
+      if (ok) ok = mbar_wait_warp(bar_kfree + j % KST, (j / KST) & 1, p.err, kErrWaitSoftmax);
+      if (ok) {
+        tc_fence_after();
+        tmem_ld32(tS + (j & 1) * 128 + lane_base + h * 64, *reinterpret_cast<uint32_t(*)[32]>(&r[0]));
+        tmem_ld32(tS + (j & 1) * 128 + lane_base + h * 64 + 32, *reinterpret_cast<uint32_t(*)[32]>(&r[32]));
+        tmem_wait_ld();
+      }
+      tc_fence_before();
+      mbar_arrive(bar_sfree + (j & 1));
+      if (ok && exact) {
+        // int32 scores -> log2 units: * (qs * s2) * ks (_int8_fwd.py:329-330)
+        const float4* ks4 = reinterpret_cast<const float4*>(sKS + (j & 3) * 128 + h * 64);
+#pragma unroll
+        for (int i = 0; i < 64; i += 4) {
+          const float4 k4 = ks4[i >> 2];
+          r[i] = __float_as_uint(i2f_exact(r[i]) * (qs_log2 * k4.x));
+          r[i + 1] = __float_as_uint(i2f_exact(r[i + 1]) * (qs_log2 * k4.y));
+          r[i + 2] = __float_as_uint(i2f_exact(r[i + 2]) * (qs_log2 * k4.z));
+          r[i + 3] = __float_as_uint(i2f_exact(r[i + 3]) * (qs_log2 * k4.w));
+        }
+      }
+      // P.V(j-1) complete: the P / P.V columns and the int8 P buffer are free again
+      bool pv_prev = j == 0;
+      auto wait_pv = [&]() {
+        if (ok && !pv_prev) {
+          ok = mbar_wait_warp(bar_vfree + (j - 1) % VST, ((j - 1) / VST) & 1, p.err, kErrWaitSoftmax);
+          tc_fence_after();
+          pv_prev = true;
+        }
+      };
+      uint32_t colmask[4];
+      int tail_col = -1;
+      bool masked = true;
+      if (!exact) {
+        it.approx_bits(idx, colmask);
+        tail_col = (p.N - 1 >= idx * 128 && p.N - 1 < idx * 128 + 128) ? p.N - 1 - idx * 128 - h * 64 : -1;
+        if (tail_col >= 64) tail_col = -1;
+      } else {
+        token_bits<128>(p.T - idx * BLK, colmask);
+        masked = idx * BLK + BLK > p.T;
+      }
+      const uint32_t cm[2] = {h ? colmask[2] : colmask[0], h ? colmask[3] : colmask[1]};
+      const float sc = exact ? 1.f : p.s2;   // scores -> log2 units
+      float pm = -INFINITY;
+      if (ok) pm = (masked ? max64<true>(r, cm) : max64<false>(r, cm)) * sc;
+      float* xm = sMax + (j & 1) * 256;
+      xm[h * 128 + row] = pm;
+      named_bar_sync(1, 256);
+      const float mx = fmaxf(pm, xm[(1 - h) * 128 + row]);   // the tile's row max
+      const float m_new = fmaxf(m_ref, mx);
+      float alpha = 1.f;
+      bool need = false;
+      if (m_ref == -INFINITY) {
+        m_ref = m_new;
+      } else if (m_new > m_ref + 8.f) {
+        alpha = fast_exp2(m_ref - m_new);
+        m_ref = m_new;
+        need = true;
+      }
+      if (exact && pv8) {
+        // ------------------------------ int8 P (relative to the tile's max) -> smem
+        const float bm = mx;
+        const float beta = mx == -INFINITY ? 0.f : fast_exp2(bm - m_ref);
+        uint32_t q[16];
+        float psum = 0.f;
+        if (ok) psum = exp_int8_64(r, bm == -INFINITY ? 0.f : bm, q);
+        l_sum = l_sum * alpha + beta * psum;
+        wait_pv();                       // int8 P buffer and P.V columns free
+        if (fold_pending) fold();        // P.V(j-1) into O before P.V(j) overwrites it
+        fold_pending = false;
+        if (ok) {
+          // this half's 64 bytes of the row: 16-byte chunks 4h..4h+3, 128-byte swizzle
+#pragma unroll
+          for (int c = 0; c < 4; ++c) {
+            const int chunk = h * 4 + c;
+            *reinterpret_cast<uint4*>(sP + row * 128 + ((chunk ^ (row & 7)) << 4)) =
+                make_uint4(q[c * 4], q[c * 4 + 1], q[c * 4 + 2], q[c * 4 + 3]);
+          }
+        }
+        fence_proxy_async_smem();        // generic stores -> tensor core (async proxy)
+        f_alpha = alpha;
+        f_scale = beta * (1.0f / 127.0f);
+        fold_pending = true;
+      } else {
+        // ------------------------------ bf16 P in TMEM, P.V accumulated by the MMA
+        if (__any_sync(0xffffffffu, need) && o_live) {
+          wait_pv();
+          l_sum *= alpha;
+          if (ok) rescale_rows<64>(tO + lane_base + h * 64, alpha);
+        }
+        const float m_use = m_ref == -INFINITY ? 0.f : m_ref;
+        float psum = 0.f;
+        if (ok)
+          psum = exact ? exp_bf16_64<false>(r, sc, m_use, -1, 0.f, 1.f)
+                       : exp_bf16_64<true>(r, sc, m_use, tail_col, (float)(p.T - (p.N - 1) * BLK), (float)BLK);
+        l_sum += psum;
+        wait_pv();                       // P columns free
+        if (ok) {
+          tmem_st32(tA + lane_base + h * 32, *reinterpret_cast<const uint32_t(*)[32]>(&r[0]));
+          tmem_wait_st();
+        }
+        o_live = true;
+      }
+      tc_fence_before();
+      mbar_arrive(bar_pfull);
+    }
+    // epilogue: the last P.V (and its fold), l = both halves' sums, O / l -> bf16 ->
+    // swizzled staging (the q buffer) -> TMA store when every softmax thread succeeded
+    if (j > 0 && ok) {
+      ok = mbar_wait_warp(bar_vfree + (j - 1) % VST, ((j - 1) / VST) & 1, p.err, kErrWaitEpilogue);
+      tc_fence_after();
+      if (fold_pending) fold();
+    }
+    sSum[h * 128 + row] = l_sum;
+    if (!ok) *sBad = 1;
+    named_bar_sync(1, 256);
+    const float inv = 1.f / (sSum[row] + sSum[128 + row]);
+    ok = ok && *sBad == 0;
+    if (ok && j > 0) {
+      uint8_t* sO = sQ;
+#pragma unroll
+      for (int c = 0; c < 2; ++c) {
+        uint32_t r[32];
+        tmem_ld32(tO + lane_base + h * 64 + c * 32, r);
+        tmem_wait_ld();
+        const int chunk0 = c * 4;   // 64 bf16 of O half h = box h, chunks 0..7
+#pragma unroll
+        for (int v4 = 0; v4 < 4; ++v4) {
+          uint4 w;
+          w.x = pack_bf16x2(__uint_as_float(r[v4 * 8 + 0]) * inv, __uint_as_float(r[v4 * 8 + 1]) * inv);
+          w.y = pack_bf16x2(__uint_as_float(r[v4 * 8 + 2]) * inv, __uint_as_float(r[v4 * 8 + 3]) * inv);
+          w.z = pack_bf16x2(__uint_as_float(r[v4 * 8 + 4]) * inv, __uint_as_float(r[v4 * 8 + 5]) * inv);
+          w.w = pack_bf16x2(__uint_as_float(r[v4 * 8 + 6]) * inv, __uint_as_float(r[v4 * 8 + 7]) * inv);
+          const int chunk = chunk0 + v4;
+          *reinterpret_cast<uint4*>(sO + h * BOX + row * 128 + ((chunk ^ (row & 7)) << 4)) = w;
+        }
+      }
+      fence_proxy_async_smem();
+    }
+    if (!ok) *sBad = 1;
+    named_bar_sync(1, 256);
+    if (threadIdx.x == 0 && j > 0 && *sBad == 0) {
+      for (int i = 0; i < 2; ++i) tma_store_4d(&tm_o, sQ + i * BOX, i * 64, u.h, u.qb * BLK, u.b);
+      bulk_commit_group();
+      bulk_wait_group_read0();
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 9) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
+// q 32 KB + qi 16 KB + K ring 64 KB + V ring 64 KB + P 16 KB + scales + barriers +
+// mask row + exchange, plus 1 KB to align the tiles to 1024 bytes
+size_t fwd_int8p_smem_bytes() {
+  return (size_t)(2 * 16384 + 16384 + 2 * 32768 + 2 * 32768 + 16384) + 4 * 128 * 4 + 128 * 4 + 128 +
+         4 * kMaskCapI8 + 4 * (512 + 256) + 16 + 1024;
+}
+
+cudaError_t launch_fwd_int8p(const FwdMaps& m, const FwdParams& p, cudaStream_t st) {
+  const size_t smem = fwd_int8p_smem_bytes();
+  cudaError_t e = cudaFuncSetAttribute(sol_fwd_int8p_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  if (e != cudaSuccess) return e;
+  const unsigned grid = (unsigned)((int64_t)p.B * p.H * p.N);
+  sol_fwd_int8p_kernel<<<grid, 320, smem, st>>>(m.q, m.kc, m.vc, m.o, m.qi, m.ki, m.vi, m.v, p);
+  return cudaGetLastError();
+}
+
+}  // namespace solb200

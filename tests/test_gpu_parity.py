@@ -280,6 +280,10 @@ def test_config3_head_slice(cuda_device):
     rows = np.concatenate([np.arange(n * 128, min(cfg.tokens, n * 128 + 128))
                            for n in range(0, cfg.blocks, 17)])
     assert_close_output(out.float().cpu().numpy()[:, rows], want[:, rows], "config 3 slice")
+    for pv in (True, False):
+        out8 = solb200.sol_attn_int8(qd, kd, vd, tau=cfg.tau, block=cfg.block, int8_pv=pv)
+        want8 = O.sol_attn_int8(qn, kn, vn, tau=cfg.tau, block=cfg.block, int8_pv=pv, units=units)
+        assert_close_output(out8.float().cpu().numpy()[:, rows], want8[:, rows], f"config 3 slice int8 pv={pv}")
     kc, vc, thr = solb200.prepare(qd, kd, vd, tau=cfg.tau, scale=128 ** -0.5, block=cfg.block)
     wkc, wvc, wthr = O.prepare(qn, kn, vn, cfg.tau, 128 ** -0.5, cfg.tokens, cfg.block)
     assert_bitexact(kc, wkc, "kc")
