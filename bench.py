@@ -206,17 +206,15 @@ def run_ours(args, rank, world, local_rank):
     fwd_flops = exact_flops + approx_flops
     dense_job = cfg.dense_flops()
 
-    # e2e through the public API: pinned host q/k/v -> device -> sol_attn -> host
+    # e2e through the public API for host-resident tensors: pinned host q/k/v ->
+    # solb200.sol_attn_host (head chunks streamed H2D / computed / streamed D2H on
+    # three streams) -> pinned host output
     hq, hk, hv = (t.cpu().pin_memory() for t in (q, k, v))
     hout = torch.empty((B, T, H, D), dtype=torch.bfloat16).pin_memory()
-    fn = solb200.sol_attn_int8 if int8 else solb200.sol_attn
 
     def e2e_step():
-        dq = hq.to(dev, non_blocking=True)
-        dk = hk.to(dev, non_blocking=True)
-        dv = hv.to(dev, non_blocking=True)
-        o = fn(dq, dk, dv, tau=cfg.tau, block=blk)
-        hout.copy_(o, non_blocking=True)
+        solb200.sol_attn_host(hq, hk, hv, tau=cfg.tau, block=blk, int8=int8, out=hout,
+                              heads_per_chunk=args.e2e_chunk or None, synchronize=False)
 
     ms_e2e = None
     if not args.no_e2e:
@@ -272,7 +270,8 @@ def run_ours(args, rank, world, local_rank):
                              f"peak = bf16 dense burst, {peaks['source']}; traffic = DRAM bytes "
                              f"per launch from the ncu capture in profiles/, scaled to {H} heads"},
         "e2e": ({"value": dense_job / (ms_e2e * 1e-3) / 1e12, "unit": UNIT, "ms_per_step": ms_e2e,
-                 "h2d_bytes_per_step": h2d * world, "d2h_bytes_per_step": d2h * world}
+                 "h2d_bytes_per_step": h2d * world, "d2h_bytes_per_step": d2h * world,
+                 "api": "solb200.sol_attn_host (pinned host in and out, head chunks streamed)"}
                 if ms_e2e else None),
         "gpu_launches": 4 * args.steps + (1 if int8 else 0) * args.steps,
         "clocks": clocks,
@@ -350,6 +349,8 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-units", type=int, default=64)
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--e2e-chunk", type=int, default=0,
+                    help="heads per streamed chunk in the e2e leg (0 = the API default)")
     ap.add_argument("--heads", type=int, default=0,
                     help="profiling only: run this many of the 40 heads (0 = all)")
     args = ap.parse_args()

@@ -426,6 +426,22 @@ int32_t solb200_gather_rows(const void* const* src, void* const* dst, int32_t nt
   return e == cudaSuccess ? SOLB200_OK : cuda_fail(e, "gather launch");
 }
 
+int32_t solb200_copy_heads(void* device, void* host, int64_t batch, int64_t tokens, int64_t heads,
+                           int64_t head_dim, int64_t h0, int64_t hc, int32_t to_device, void* stream) {
+  if (!device || !host) return fail(SOLB200_ERR_INVALID, "null pointer");
+  if (batch < 1 || tokens < 1 || heads < 1 || head_dim < 1 || hc < 1 || h0 < 0 || h0 + hc > heads)
+    return fail(SOLB200_ERR_INVALID, "head range [h0, h0+hc) must lie in [0, heads)");
+  const size_t esz = 2;   // bf16
+  const size_t host_pitch = (size_t)heads * head_dim * esz, dev_pitch = (size_t)hc * head_dim * esz;
+  const size_t width = dev_pitch, height = (size_t)batch * tokens;
+  char* h = static_cast<char*>(host) + (size_t)h0 * head_dim * esz;
+  const cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const cudaError_t e = to_device
+      ? cudaMemcpy2DAsync(device, dev_pitch, h, host_pitch, width, height, cudaMemcpyHostToDevice, st)
+      : cudaMemcpy2DAsync(h, host_pitch, device, dev_pitch, width, height, cudaMemcpyDeviceToHost, st);
+  return e == cudaSuccess ? SOLB200_OK : cuda_fail(e, "cudaMemcpy2DAsync (head chunk)");
+}
+
 }  // extern "C"
 
 namespace solb200 {

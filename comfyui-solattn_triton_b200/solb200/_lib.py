@@ -51,6 +51,8 @@ _SIGS = {
     "solb200_read_device_error": (c_int32, [c_void_p, POINTER(c_int32), c_void_p]),
     "solb200_morton_perm": (c_int32, [c_int64, c_int64, c_int64, c_int32, c_int64, c_void_p, c_void_p,
                                       c_void_p]),
+    "solb200_copy_heads": (c_int32, [c_void_p, c_void_p, c_int64, c_int64, c_int64, c_int64, c_int64, c_int64,
+                                     c_int32, c_void_p]),
     "solb200_gather_rows": (c_int32, [POINTER(c_void_p), POINTER(c_void_p), c_int32, c_void_p, c_int64,
                                       c_int64, c_int64, c_int64, c_int64, c_int64, c_int64, c_void_p]),
 }

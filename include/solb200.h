@@ -149,6 +149,17 @@ SOLB200_API int32_t solb200_read_device_error(void* workspace, int32_t* code, vo
 SOLB200_API int32_t solb200_morton_perm(int64_t frames, int64_t height, int64_t width, int32_t curve,
                             int64_t roll, int64_t* perm, int64_t* inverse, void* stream);
 
+/* Copy heads [h0, h0+hc) of a bf16 BTHD tensor between a host array [B, T, H, D]
+ * (head_dim contiguous, dense) and a dense device array [B, T, hc, D], as one strided
+ * 2-D copy on `stream`: to_device = 1 copies host -> device, 0 device -> host. With a
+ * page-locked host array the copy is asynchronous and overlaps kernels and copies in the
+ * other direction. No counterpart in the reference (it is handed device tensors); it
+ * lets a caller holding q/k/v in host memory stream them through the GPU head chunk by
+ * head chunk (solb200.sol_attn_host). */
+SOLB200_API int32_t solb200_copy_heads(void* device, void* host, int64_t batch, int64_t tokens, int64_t heads,
+                                       int64_t head_dim, int64_t h0, int64_t hc, int32_t to_device,
+                                       void* stream);
+
 /* dst[b, i, :] = src[b, index[i], :] for up to 4 tensors that share one geometry:
  * rows of row_bytes (a multiple of 16) with byte strides {batch, row}. */
 SOLB200_API int32_t solb200_gather_rows(const void* const* src, void* const* dst, int32_t ntensors,
