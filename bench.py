@@ -241,6 +241,31 @@ def run_ours(args, rank, world, local_rank):
         except Exception as exc:   # pragma: no cover - informational only
             ms_dense = f"failed: {exc}"
 
+    # Morton (both curves): reorder cost, routed density and accuracy against dense SDPA,
+    # next to the unpermuted call (one GPU only; needs the dense output)
+    morton = None
+    if world == 1 and isinstance(ms_dense, float):
+        fn = solb200.sol_attn_int8 if int8 else solb200.sol_attn
+        dense_out = sdpa(qt, kt, vt).transpose(1, 2)
+
+        def vs_dense(o):
+            a, b = o.float().flatten(), dense_out.float().flatten()
+            return {"max_abs": float((a - b).abs().max()),
+                    "cosine": float((a @ b) / (a.norm() * b.norm()))}
+
+        morton = {"none": {"routed_density": density, "vs_dense": vs_dense(fn(q, k, v, tau=cfg.tau, block=blk))}}
+        for curve in ("3d", "2d_frame"):
+            pm, ivm = solb200.morton_perm(cfg.grid, dev, curve)
+            ms_r = timed(lambda: (solb200.permute_tokens_many([q, k, v], pm),
+                                  solb200.permute_tokens(out, ivm)), 3)
+            qp, kp, vp = solb200.permute_tokens_many([q, k, v], pm)
+            r = solb200.routing(qp, kp, vp, tau=cfg.tau, block=blk, int8=int8)
+            om = solb200.permute_tokens(fn(qp, kp, vp, tau=cfg.tau, block=blk), ivm)
+            morton[curve] = {"reorder_ms": ms_r, "routed_density": float(r["mask"].float().mean()),
+                             "vs_dense": vs_dense(om)}
+            del qp, kp, vp, r, om
+        del dense_out
+
     peaks = load_peaks()
     achieved = fwd_flops / (ms_fwd * 1e-3) / 1e12
     result = {
@@ -261,6 +286,7 @@ def run_ours(args, rank, world, local_rank):
                    "l2": "inputs larger than L2 (3 x 335 MB)", "routed_density": density},
         "stages_ms": {"prep_route": ms_prep, "forward": ms_fwd, "reorder_qkv_and_o": ms_reorder},
         "dense_sdpa_ms": ms_dense,
+        "morton": morton,
         "sparse_over_dense": (ms / ms_dense) if isinstance(ms_dense, float) else None,
         "roofline": {"bound": "tensor", "kernel": "sol_fwd_%s_kernel" % ("int8" if int8 else "bf16"),
                      "achieved": achieved, "peak": peaks["bf16"], "unit": "TFLOP/s",

@@ -298,3 +298,49 @@ def test_bad_arguments_raise(cuda_device):
     q = torch.zeros(1, 256, 2, 64, dtype=torch.float16, device=cuda_device)
     with pytest.raises(RuntimeError, match="bfloat16"):
         solb200.sol_attn(q, q, q)
+
+
+def _slice_inputs(cfg_name, heads):
+    """One or two heads of a config's seeded tensors, drawn on the GPU (the full draw
+    of the long configs is slow on the host), plus host copies for the oracle."""
+    cfg = CONFIGS[cfg_name]
+    qd, kd, vd = make_qkv(cfg, device="cuda", heads=heads)
+    qd, kd, vd = (t.contiguous() for t in (qd, kd, vd))
+    qn, kn, vn = (O.to_np(t.cpu()) for t in (qd, kd, vd))
+    return cfg, (qd, kd, vd), (qn, kn, vn)
+
+
+def _sampled(cfg, step, nheads):
+    units = [(0, h, n) for h in range(nheads) for n in range(0, cfg.blocks, step)]
+    rows = np.concatenate([np.arange(n * cfg.block, min(cfg.tokens, n * cfg.block + cfg.block))
+                           for n in range(0, cfg.blocks, step)])
+    return units, rows
+
+
+@pytest.mark.parametrize("tau", [0.8, 0.9, 0.95])
+def test_config4_int8_head_slice(cuda_device, tau):
+    """Config 4 (720p, T = 75600, INT8 at the three taus of the config) on one head:
+    forward on sampled query blocks and the full routing mask against the oracle."""
+    cfg, (qd, kd, vd), (qn, kn, vn) = _slice_inputs("c4", slice(3, 4))
+    units, rows = _sampled(cfg, 41, 1)
+    out8 = solb200.sol_attn_int8(qd, kd, vd, tau=tau, block=cfg.block)
+    want8 = O.sol_attn_int8(qn, kn, vn, tau=tau, block=cfg.block, units=units)
+    assert_close_output(out8.float().cpu().numpy()[:, rows], want8[:, rows], f"config 4 int8 tau={tau}")
+    r = solb200.routing(qd, kd, vd, tau=tau, block=cfg.block, int8=True)
+    parts = O.fused_preprocess(qn, kn, vn, tau, 128 ** -0.5, cfg.tokens, cfg.block)
+    want, stat = O.route_mask(qn, parts["kc"], parts["thr"], 128 ** -0.5, cfg.tokens, cfg.block)
+    flips = assert_mask_parity(r["mask"], want, stat, parts["thr"], f"config 4 tau={tau}")
+    assert flips <= 2
+
+
+def test_config5_head_slice(cuda_device):
+    """Config 5 (T = 111600, N = 872 blocks) on one head, BF16 and INT8, sampled query
+    blocks against the oracle."""
+    cfg, (qd, kd, vd), (qn, kn, vn) = _slice_inputs("c5", slice(7, 8))
+    units, rows = _sampled(cfg, 67, 1)
+    out = solb200.sol_attn(qd, kd, vd, tau=cfg.tau, block=cfg.block)
+    want = O.sol_attn(qn, kn, vn, tau=cfg.tau, block=cfg.block, units=units)
+    assert_close_output(out.float().cpu().numpy()[:, rows], want[:, rows], "config 5 bf16")
+    out8 = solb200.sol_attn_int8(qd, kd, vd, tau=cfg.tau, block=cfg.block)
+    want8 = O.sol_attn_int8(qn, kn, vn, tau=cfg.tau, block=cfg.block, units=units)
+    assert_close_output(out8.float().cpu().numpy()[:, rows], want8[:, rows], "config 5 int8")
