@@ -364,7 +364,29 @@ def cpu_baseline(path, procs, budget_units):
 
 # --------------------------------------------------------------------- main
 
+# stdout carries exactly one line, the JSON result: everything else written to file
+# descriptor 1 (NCCL's version banner, library chatter, stray prints) goes to stderr
+_RESULT_FD = None
+
+
+def _isolate_stdout():
+    global _RESULT_FD
+    sys.stdout.flush()
+    _RESULT_FD = os.dup(1)
+    os.dup2(2, 1)
+
+
+def emit(obj):
+    line = (json.dumps(obj) + "\n").encode()
+    if _RESULT_FD is None:
+        sys.stdout.write(line.decode())
+        sys.stdout.flush()
+    else:
+        os.write(_RESULT_FD, line)
+
+
 def main():
+    _isolate_stdout()
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=10)
@@ -398,7 +420,7 @@ def main():
             times.append(ms)
         ms = statistics.median(times)
         val = cfg.dense_flops() / (ms * 1e-3) / 1e12
-        print(json.dumps({
+        emit({
             "impl": "reference", "metric": METRIC, "value": val, "unit": UNIT, "n_gpus": args.gpus,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
             "scaling": "strong", "vs_baseline": None, "dtype": args.path,
@@ -408,7 +430,7 @@ def main():
             "cpu_baseline": {"value": val, "unit": UNIT, "cores": info["cores"], "kind": "port",
                              "sample": info["sample"]},
             "e2e": {"value": val, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
-        }))
+        })
         return
 
     import torch
@@ -434,7 +456,7 @@ def main():
                 "ms_per_call": ms_cpu}
         except Exception as exc:   # pragma: no cover
             result["cpu_baseline"] = {"error": str(exc)}
-    print(json.dumps(result))
+    emit(result)
 
 
 if __name__ == "__main__":

@@ -30,7 +30,7 @@ struct Plan {
   int64_t B, T, H, D;
   int blk, N, npad, nw;
   bool int8;
-  int64_t off[16];
+  int64_t off[17];
   int64_t total;
 };
 
@@ -71,6 +71,7 @@ int32_t make_plan(int64_t B, int64_t T, int64_t H, int64_t D, int32_t blk, int32
     p.off[SOLB200_BUF_KS] = take(B * H * (int64_t)p.N * blk * 4);
     p.off[SOLB200_BUF_VI] = take(B * T * H * D);
   }
+  p.off[SOLB200_BUF_ORDER] = take(B * H * p.N * 4);
   p.total = cur;
   return SOLB200_OK;
 }
@@ -245,13 +246,17 @@ int32_t run(const Plan& P, const Call& c) {
   auto clampi = [&](int64_t x) { return (int)(x < -lim ? -lim : (x > lim ? lim : x)); };
   rp.sink_kv0 = clampi(c.sink_kv[0]); rp.sink_kv1 = clampi(c.sink_kv[1]);
   rp.sink_q0 = clampi(c.sink_q[0]); rp.sink_q1 = clampi(c.sink_q[1]);
-  if (prep) launch_route(rp, hd, c.st);
+  if (prep) {
+    launch_route(rp, hd, c.st);
+    launch_order(rp.count, at<int>(c.ws, P, SOLB200_BUF_ORDER), (int)(P.B * P.H), P.N, c.st);
+  }
   e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, "preprocess launch");
   if (c.stages == SOLB200_STAGES_PREPARE) return SOLB200_OK;
 
   FwdParams fp{};
   fp.mask = rp.mask;
+  fp.order = at<int>(c.ws, P, SOLB200_BUF_ORDER);
   fp.err = err;
   fp.B = (int)P.B; fp.T = (int)P.T; fp.H = (int)P.H; fp.N = P.N; fp.nw = P.nw;
   fp.s2 = s2;
@@ -320,7 +325,7 @@ int32_t solb200_workspace_offset(int64_t batch, int64_t tokens, int64_t heads, i
   Plan p;
   const int32_t rc = make_plan(batch, tokens, heads, head_dim, block, int8, p);
   if (rc) return rc;
-  if (which < 0 || which > SOLB200_BUF_VI || p.off[which] < 0)
+  if (which < 0 || which > SOLB200_BUF_ORDER || p.off[which] < 0)
     return fail(SOLB200_ERR_INVALID, "buffer not part of this workspace");
   if (!offset) return fail(SOLB200_ERR_INVALID, "offset: null pointer");
   *offset = p.off[which];

@@ -7,6 +7,7 @@ namespace solb200 {
 
 struct FwdParams {
   const uint32_t* mask;   // [B, H, N, nw] exact-block bits (routing output)
+  const int* order;       // [B*H*N] unit of each CTA (the schedule), or null: CTA i = unit i
   int* err;               // device error word
   int B, T, H, N, nw;
   float s2;               // softmax scale * log2(e)
@@ -28,9 +29,12 @@ struct UnitInfo {
                          // copy, so they are read with generic (not ld.global.nc) loads
 };
 
-// Units are numbered head-major, (b*H + h)*N + qb, so CTAs that run together share
-// a head's K/V in L2.
-__device__ __forceinline__ UnitInfo decode_unit(const FwdParams& p, int unit) {
+// Units are numbered head-major, (b*H + h)*N + qb. CTA i runs unit order[i]: the
+// schedule keeps heads in order, so CTAs that run together share a head's K/V in L2,
+// and within a head runs the query blocks with the most exact blocks first, so the
+// grid's last wave is made of its shortest units.
+__device__ __forceinline__ UnitInfo decode_unit(const FwdParams& p, int cta) {
+  const int unit = p.order ? __ldg(p.order + cta) : cta;
   UnitInfo u;
   u.qb = unit % p.N;
   const int bh = unit / p.N;

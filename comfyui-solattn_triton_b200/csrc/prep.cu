@@ -510,6 +510,58 @@ void launch_moments(const MomentsParams& p, int hd, bool int8, cudaStream_t st) 
   }
 }
 
+// ------------------------------------------------------------------- schedule
+
+// One CTA per (b, h): counting sort of the head's query blocks by exact-block count,
+// descending (counts above 1023 share the top bin). The order inside a bin does not
+// matter: every unit's output is independent of when it runs.
+__global__ void __launch_bounds__(256) order_kernel(const int* __restrict__ count, int* __restrict__ order,
+                                                    int n) {
+  constexpr int kBins = 1024;
+  __shared__ int hist[kBins];
+  __shared__ int warp_tot[8];
+  const int bh = blockIdx.x;
+  const int* c = count + (int64_t)bh * n;
+  int* o = order + (int64_t)bh * n;
+  for (int i = threadIdx.x; i < kBins; i += 256) hist[i] = 0;
+  __syncthreads();
+  for (int i = threadIdx.x; i < n; i += 256) atomicAdd(&hist[kBins - 1 - min(c[i], kBins - 1)], 1);
+  __syncthreads();
+  // exclusive prefix sum of the bins (bin 0 = largest count): 4 bins per thread
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  int v[4], s = 0;
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {
+    v[k] = hist[threadIdx.x * 4 + k];
+    s += v[k];
+  }
+  int incl = s;
+#pragma unroll
+  for (int off = 1; off < 32; off <<= 1) {
+    const int y = __shfl_up_sync(0xffffffffu, incl, off);
+    if (lane >= off) incl += y;
+  }
+  if (lane == 31) warp_tot[warp] = incl;
+  __syncthreads();
+  int base = 0;
+  for (int w = 0; w < warp; ++w) base += warp_tot[w];
+  int run = base + incl - s;
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {
+    hist[threadIdx.x * 4 + k] = run;
+    run += v[k];
+  }
+  __syncthreads();
+  for (int i = threadIdx.x; i < n; i += 256) {
+    const int pos = atomicAdd(&hist[kBins - 1 - min(c[i], kBins - 1)], 1);
+    o[pos] = bh * n + i;
+  }
+}
+
+void launch_order(const int* count, int* order, int bh_count, int n, cudaStream_t st) {
+  order_kernel<<<bh_count, 256, 0, st>>>(count, order, n);
+}
+
 void launch_route(const RouteParams& p, int hd, cudaStream_t st) {
   dim3 grid((p.N + 7) / 8, p.B * p.H);
   if (hd == 128) route_kernel<128><<<grid, 256, 0, st>>>(p);

@@ -63,6 +63,8 @@ struct GatherParams {
 void launch_pool(const PoolParams& p, int hd, bool vamax, bool qquant, cudaStream_t st);
 void launch_moments(const MomentsParams& p, int hd, bool int8, cudaStream_t st);
 void launch_route(const RouteParams& p, int hd, cudaStream_t st);
+// order[bh*N ..] = the units of head bh, its query blocks by descending count
+void launch_order(const int* count, int* order, int bh_count, int n, cudaStream_t st);
 void launch_quant_kv(const QuantParams& p, int hd, cudaStream_t st);
 void launch_morton(int64_t frames, int64_t height, int64_t width, int curve, int64_t roll,
                    int64_t* perm, int64_t* inverse, cudaStream_t st);

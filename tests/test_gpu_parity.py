@@ -344,3 +344,21 @@ def test_config5_head_slice(cuda_device):
     out8 = solb200.sol_attn_int8(qd, kd, vd, tau=cfg.tau, block=cfg.block)
     want8 = O.sol_attn_int8(qn, kn, vn, tau=cfg.tau, block=cfg.block, units=units)
     assert_close_output(out8.float().cpu().numpy()[:, rows], want8[:, rows], "config 5 int8")
+
+
+def test_forward_schedule(cuda_device):
+    """The forward's unit schedule: head by head, each head's query blocks once, by
+    non-increasing exact-block count."""
+    from solb200.ops import STAGES_PREPARE, _attn
+    g, (B, T, H, D, blk), (q, k, v) = _golden_inputs("groups")
+    _, ws, _, _ = _attn(q, k, v, scale=None, tau=0.5, sink_blocks=(0, 0), sink_q=(0, 0), block=blk,
+                        int8=False, int8_pv=False, stages=STAGES_PREPARE)
+    N = ws.N
+    order = ws.view("order", torch.int32, (B * H * N,)).cpu().numpy()
+    counts = ws.view("count", torch.int32, (B * H * N,)).cpu().numpy()
+    for bh in range(B * H):
+        seg = order[bh * N:(bh + 1) * N]
+        assert sorted(seg.tolist()) == list(range(bh * N, (bh + 1) * N))
+        c = counts[seg]
+        assert (np.diff(c) <= 0).all(), "query blocks not by descending count"
+    assert counts.min() < counts.max(), "fixture should have uneven counts"
