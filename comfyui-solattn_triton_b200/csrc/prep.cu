@@ -42,58 +42,63 @@ __device__ __forceinline__ int round_half_away(float x) {
   return x >= 0.f ? __float2int_rz(__fadd_rn(x, 0.5f)) : __float2int_rz(__fsub_rn(x, 0.5f));
 }
 
-// One thread owns 8 consecutive channels (16 bytes) of one head; a CTA covers
-// 128 * 8 channels of one (batch, block). Rows are accumulated in token order
-// (row 0 first) in fp32, which is the order of the reference's block sums.
-// Grid: (ceil(H*D/8 / 128), Npad, B).
+// One thread owns 8 consecutive channels (16 bytes) of one head and one of the three
+// tensors (role 0: Q -> centroid and, for INT8, qi / qs; role 1: K -> kc; role 2:
+// V -> vc and |V| max), so a call with few heads still has three threads per channel
+// group in flight. Rows are accumulated in token order (row 0 first) in fp32, the
+// order of the reference's block sums. Grid: (ceil(H*D/8 / 64), Npad, 3*B); 64 threads.
 template <int HD, bool VAMAX, bool QQUANT>
-__global__ void __launch_bounds__(128) pool_kernel(PoolParams p) {
+__global__ void __launch_bounds__(64) pool_kernel(PoolParams p) {
   constexpr int LANES_PER_HEAD = HD / 8;
-  const int g = blockIdx.x * 128 + threadIdx.x;
-  const int n = blockIdx.y, b = blockIdx.z;
+  const int g = blockIdx.x * 64 + threadIdx.x;
+  const int n = blockIdx.y, b = blockIdx.z / 3, role = blockIdx.z % 3;
   const bool active = g < p.H * LANES_PER_HEAD;
   const int h = g / LANES_PER_HEAD;
   const int d0 = (g % LANES_PER_HEAD) * 8;
   const int64_t out_off = (((int64_t)b * p.npad + n) * p.H + h) * HD + d0;
   if (n >= p.N) {   // zero padding rows of kc / vc
-    if (active) {
-      *reinterpret_cast<uint4*>(p.kc + out_off) = make_uint4(0, 0, 0, 0);
-      *reinterpret_cast<uint4*>(p.vc + out_off) = make_uint4(0, 0, 0, 0);
-    }
+    if (active && role > 0)
+      *reinterpret_cast<uint4*>((role == 1 ? p.kc : p.vc) + out_off) = make_uint4(0, 0, 0, 0);
     return;
   }
   const int r0 = n * p.blk;
   const int r1 = min(p.T, r0 + p.blk);
-  float ks[8], vs[8], qsum[8], vmax[8];
+  const __nv_bfloat16* src;
+  int64_t st;
+  if (role == 0) {
+    src = p.q + (int64_t)b * p.sq_b + (int64_t)h * p.sq_h + d0;
+    st = p.sq_t;
+  } else if (role == 1) {
+    src = p.k + (int64_t)b * p.sk_b + (int64_t)h * p.sk_h + d0;
+    st = p.sk_t;
+  } else {
+    src = p.v + (int64_t)b * p.sv_b + (int64_t)h * p.sv_h + d0;
+    st = p.sv_t;
+  }
+  float sum[8], vmax[8];
 #pragma unroll
-  for (int i = 0; i < 8; ++i) ks[i] = vs[i] = qsum[i] = vmax[i] = 0.f;
-  const __nv_bfloat16* qp = p.q + (int64_t)b * p.sq_b + (int64_t)h * p.sq_h + d0;
-  const __nv_bfloat16* kp = p.k + (int64_t)b * p.sk_b + (int64_t)h * p.sk_h + d0;
-  const __nv_bfloat16* vp = p.v + (int64_t)b * p.sv_b + (int64_t)h * p.sv_h + d0;
-#pragma unroll 4
+  for (int i = 0; i < 8; ++i) sum[i] = vmax[i] = 0.f;
+#pragma unroll 8
   for (int r = r0; r < r1; ++r) {
-    float xq[8], xk[8], xv[8];
+    float x[8];
     if (active) {
-      load8(qp + (int64_t)r * p.sq_t, xq);
-      load8(kp + (int64_t)r * p.sk_t, xk);
-      load8(vp + (int64_t)r * p.sv_t, xv);
+      load8(src + (int64_t)r * st, x);
     } else {
 #pragma unroll
-      for (int i = 0; i < 8; ++i) xq[i] = xk[i] = xv[i] = 0.f;
+      for (int i = 0; i < 8; ++i) x[i] = 0.f;
     }
 #pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      ks[i] = __fadd_rn(ks[i], xk[i]);
-      vs[i] = __fadd_rn(vs[i], xv[i]);
-      qsum[i] = __fadd_rn(qsum[i], xq[i]);
-      if (VAMAX) vmax[i] = fmaxf(vmax[i], fabsf(xv[i]));
+    for (int i = 0; i < 8; ++i) sum[i] = __fadd_rn(sum[i], x[i]);
+    if (VAMAX && role == 2) {
+#pragma unroll
+      for (int i = 0; i < 8; ++i) vmax[i] = fmaxf(vmax[i], fabsf(x[i]));
     }
-    if (QQUANT) {
+    if (QQUANT && role == 0) {
       // per-token symmetric int8 of Q (_fused_prep.py:36-44): s = max|x| / 127,
       // floor at 1e-8, clamp(x / s, +-127), round half away from zero.
       float amax = 0.f;
 #pragma unroll
-      for (int i = 0; i < 8; ++i) amax = fmaxf(amax, fabsf(xq[i]));
+      for (int i = 0; i < 8; ++i) amax = fmaxf(amax, fabsf(x[i]));
 #pragma unroll
       for (int off = 1; off < LANES_PER_HEAD; off <<= 1)
         amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, off));
@@ -103,8 +108,8 @@ __global__ void __launch_bounds__(128) pool_kernel(PoolParams p) {
         uint32_t lo = 0, hi = 0;
 #pragma unroll
         for (int i = 0; i < 8; ++i) {
-          float x = fminf(fmaxf(__fdiv_rn(xq[i], s_safe), -127.f), 127.f);
-          const uint32_t byte = (uint32_t)(round_half_away(x) & 0xff);
+          float xv = fminf(fmaxf(__fdiv_rn(x[i], s_safe), -127.f), 127.f);
+          const uint32_t byte = (uint32_t)(round_half_away(xv) & 0xff);
           if (i < 4) lo |= byte << (8 * i); else hi |= byte << (8 * (i - 4));
         }
         const int64_t qo = (((int64_t)b * p.T + r) * p.H + h) * HD + d0;
@@ -115,24 +120,25 @@ __global__ void __launch_bounds__(128) pool_kernel(PoolParams p) {
   }
   if (!active) return;
   const float len = (float)(r1 - r0);
-  float kcv[8], vcv[8];
-#pragma unroll
-  for (int i = 0; i < 8; ++i) {
-    kcv[i] = __fdiv_rn(bf16_round(ks[i]), len);   // bf16 block sum, then / len
-    vcv[i] = vs[i];
-  }
-  *reinterpret_cast<uint4*>(p.kc + out_off) = pack8_bf16(kcv);
-  *reinterpret_cast<uint4*>(p.vc + out_off) = pack8_bf16(vcv);
   const int64_t c_off = (((int64_t)b * p.N + n) * p.H + h) * HD + d0;
-  float4* cp = reinterpret_cast<float4*>(p.centroid + c_off);
-  cp[0] = make_float4(__fdiv_rn(qsum[0], len), __fdiv_rn(qsum[1], len),
-                      __fdiv_rn(qsum[2], len), __fdiv_rn(qsum[3], len));
-  cp[1] = make_float4(__fdiv_rn(qsum[4], len), __fdiv_rn(qsum[5], len),
-                      __fdiv_rn(qsum[6], len), __fdiv_rn(qsum[7], len));
-  if (VAMAX) {
-    float4* ap = reinterpret_cast<float4*>(p.vamax + c_off);
-    ap[0] = make_float4(vmax[0], vmax[1], vmax[2], vmax[3]);
-    ap[1] = make_float4(vmax[4], vmax[5], vmax[6], vmax[7]);
+  if (role == 0) {
+    float4* cp = reinterpret_cast<float4*>(p.centroid + c_off);
+    cp[0] = make_float4(__fdiv_rn(sum[0], len), __fdiv_rn(sum[1], len),
+                        __fdiv_rn(sum[2], len), __fdiv_rn(sum[3], len));
+    cp[1] = make_float4(__fdiv_rn(sum[4], len), __fdiv_rn(sum[5], len),
+                        __fdiv_rn(sum[6], len), __fdiv_rn(sum[7], len));
+  } else if (role == 1) {
+    float kcv[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) kcv[i] = __fdiv_rn(bf16_round(sum[i]), len);   // bf16 block sum, then / len
+    *reinterpret_cast<uint4*>(p.kc + out_off) = pack8_bf16(kcv);
+  } else {
+    *reinterpret_cast<uint4*>(p.vc + out_off) = pack8_bf16(sum);
+    if (VAMAX) {
+      float4* ap = reinterpret_cast<float4*>(p.vamax + c_off);
+      ap[0] = make_float4(vmax[0], vmax[1], vmax[2], vmax[3]);
+      ap[1] = make_float4(vmax[4], vmax[5], vmax[6], vmax[7]);
+    }
   }
 }
 
@@ -183,66 +189,148 @@ __device__ __forceinline__ float pairwise_sum(F x) {
 }
 
 
-// One CTA per (b, h), one thread per channel.
+// ATen's cascade sum (above) of `count` values in parallel, bit for bit: level 0 always
+// restarts from zero, so each chunk of 2^lp values can be summed by its own thread in
+// order; one thread per channel then replays the level folds over the chunk sums and
+// adds the tail. x(n, d) gives value n of channel d; the result for channel d is
+// written to out[d]. Called by all NT threads of the CTA.
+template <int HD, int NT, typename F>
+__device__ void cascade_sum_par(int count, F x, float* s_chunk /* [64][HD] */, float* out) {
+  int lp = 0;
+  while ((1 << lp) < count) ++lp;
+  lp = max(4, lp / 4);
+  const int step = 1 << lp;            // <= 64 for count < 2^24
+  const int mask = step - 1;
+  const int full = count / step;       // chunks taken by the cascade's main loop
+  const int d = threadIdx.x;           // the folding thread of channel d (d < HD)
+  float acc1 = 0.f, acc2 = 0.f, acc3 = 0.f;
+  for (int g0 = 0; g0 < full; g0 += step) {
+    const int gn = min(step, full - g0);   // chunks in this group
+    for (int it = threadIdx.x; it < gn * HD; it += NT) {
+      const int c = it / HD, dd = it % HD;
+      const int n0 = (g0 + c) * step;
+      float a = 0.f;
+      for (int j = 0; j < step; ++j) a = __fadd_rn(a, x(n0 + j, dd));
+      s_chunk[c * HD + dd] = a;
+    }
+    __syncthreads();
+    if (d < HD) {
+      for (int c = 0; c < gn; ++c) {
+        const int i = (g0 + c + 1) * step;   // values consumed after this chunk
+        acc1 = __fadd_rn(acc1, s_chunk[c * HD + d]);
+        if ((i & (mask << lp)) != 0) continue;
+        acc2 = __fadd_rn(acc2, acc1);
+        acc1 = 0.f;
+        if ((i & (mask << (2 * lp))) != 0) continue;
+        acc3 = __fadd_rn(acc3, acc2);
+        acc2 = 0.f;
+      }
+    }
+    __syncthreads();
+  }
+  if (d < HD) {
+    float tail = 0.f;
+    for (int n = full * step; n < count; ++n) tail = __fadd_rn(tail, x(n, d));
+    out[d] = __fadd_rn(__fadd_rn(__fadd_rn(tail, acc1), acc2), acc3);
+  }
+  __syncthreads();
+}
+
+// One CTA per (b, h), 512 threads.
 // BF16 mode (_preprocess.py:240-243, 149-164): kcm = mean_n kc, kcv = mean_n (kc-kcm)^2,
 //   thr = (c.kcm)*s2 + tau*sqrt(max((c^2.kcv)*s2^2, 0) + 1e-6).
 // INT8 mode (_fused_prep.py:77-81, 50-59; _fused_quant.py:103): k_mean = mean_n kc,
 //   kc <- bf16(kc - k_mean), kcv = mean_n kc^2, vscale = max(amax/127, 1e-8),
 //   thr = tau*sqrt((c^2.kcv)*s2^2 + 1e-6).
+// The D-sums of the threshold follow numpy's 8-way pairwise order: lane j of an 8-lane
+// group runs partial sum j, and three xor shuffles combine them as
+// ((r0+r1)+(r2+r3))+((r4+r5)+(r6+r7)).
 template <int HD, bool INT8>
-__global__ void __launch_bounds__(HD) moments_kernel(MomentsParams p) {
+__global__ void __launch_bounds__(512) moments_kernel(MomentsParams p) {
+  constexpr int NT = 512;
+  __shared__ float s_chunk[64 * HD];
   __shared__ float s_mean[HD], s_var[HD];
   const int bh = blockIdx.x;
   const int b = bh / p.H, h = bh % p.H;
-  const int d = threadIdx.x;
   const int64_t row = (int64_t)p.H * HD;
-  __nv_bfloat16* kcol = p.kc + ((int64_t)b * p.npad) * row + (int64_t)h * HD + d;
-  auto kc_at = [&](int n) { return __bfloat162float(kcol[(int64_t)n * row]); };
+  __nv_bfloat16* kc0 = p.kc + ((int64_t)b * p.npad) * row + (int64_t)h * HD;
+  auto kc_at = [&](int n, int d) { return __bfloat162float(kc0[(int64_t)n * row + d]); };
   const float inv_n = (float)p.N;
-  const float mean = __fdiv_rn(cascade_sum(p.N, kc_at), inv_n);
-  float var;
+  cascade_sum_par<HD, NT>(p.N, kc_at, s_chunk, s_mean);
+  if (threadIdx.x < HD) s_mean[threadIdx.x] = __fdiv_rn(s_mean[threadIdx.x], inv_n);
+  __syncthreads();
   if (INT8) {
-    for (int n = 0; n < p.N; ++n)
-      kcol[(int64_t)n * row] = __float2bfloat16_rn(__fsub_rn(kc_at(n), mean));
-    var = __fdiv_rn(cascade_sum(p.N, [&](int n) {
-                      const float x = kc_at(n);
-                      return __fmul_rn(x, x);
-                    }),
-                    inv_n);
+    for (int it = threadIdx.x; it < p.N * HD; it += NT) {
+      const int n = it / HD, d = it % HD;
+      kc0[(int64_t)n * row + d] = __float2bfloat16_rn(__fsub_rn(kc_at(n, d), s_mean[d]));
+    }
+    __syncthreads();
+    cascade_sum_par<HD, NT>(p.N, [&](int n, int d) {
+      const float x = kc_at(n, d);
+      return __fmul_rn(x, x);
+    }, s_chunk, s_var);
     if (p.vamax) {
+      // |V| max over the blocks: order-free, partial maxima over row strips
+      float* s_max = s_chunk;
+      constexpr int STRIPS = NT / HD;
+      const int d = threadIdx.x % HD, strip = threadIdx.x / HD;
       const float* vam = p.vamax + ((int64_t)b * p.N) * row + (int64_t)h * HD + d;
       float amax = 0.f;
-      for (int n = 0; n < p.N; ++n) amax = fmaxf(amax, vam[(int64_t)n * row]);
-      p.vscale[(int64_t)bh * HD + d] = fmaxf(__fdiv_rn(amax, 127.f), 1e-8f);
+      for (int n = strip; n < p.N; n += STRIPS) amax = fmaxf(amax, vam[(int64_t)n * row]);
+      s_max[strip * HD + d] = amax;
+      __syncthreads();
+      if (threadIdx.x < HD) {
+        float m = 0.f;
+        for (int k = 0; k < STRIPS; ++k) m = fmaxf(m, s_max[k * HD + threadIdx.x]);
+        p.vscale[(int64_t)bh * HD + threadIdx.x] = fmaxf(__fdiv_rn(m, 127.f), 1e-8f);
+      }
     }
   } else {
-    var = __fdiv_rn(cascade_sum(p.N, [&](int n) {
-                      const float x = __fsub_rn(kc_at(n), mean);
-                      return __fmul_rn(x, x);
-                    }),
-                    inv_n);
+    cascade_sum_par<HD, NT>(p.N, [&](int n, int d) {
+      const float x = __fsub_rn(kc_at(n, d), s_mean[d]);
+      return __fmul_rn(x, x);
+    }, s_chunk, s_var);
   }
-  p.kmean[(int64_t)bh * HD + d] = mean;
-  p.kvar[(int64_t)bh * HD + d] = var;
-  s_mean[d] = mean;
-  s_var[d] = var;
+  if (threadIdx.x < HD) {
+    s_var[threadIdx.x] = __fdiv_rn(s_var[threadIdx.x], inv_n);
+    p.kmean[(int64_t)bh * HD + threadIdx.x] = s_mean[threadIdx.x];
+    p.kvar[(int64_t)bh * HD + threadIdx.x] = s_var[threadIdx.x];
+  }
   __syncthreads();
+  // thresholds: 8 lanes per query block, 4 blocks per warp, 64 per pass of the CTA
   const float s2sq = __fmul_rn(p.s2, p.s2);
-  for (int n = threadIdx.x; n < p.N; n += HD) {
-    const float* c = p.centroid + (((int64_t)b * p.N + n) * p.H + h) * HD;
-    const float v = __fmul_rn(pairwise_sum<HD>([&](int i) {
-                                return __fmul_rn(__fmul_rn(c[i], c[i]), s_var[i]);
-                              }),
-                              s2sq);
-    float t;
-    if (INT8) {
-      t = __fmul_rn(p.tau, __fsqrt_rn(__fadd_rn(v, 1.0e-6f)));
-    } else {
-      const float m = __fmul_rn(pairwise_sum<HD>([&](int i) { return __fmul_rn(c[i], s_mean[i]); }),
-                                p.s2);
-      t = __fadd_rn(m, __fmul_rn(p.tau, __fsqrt_rn(__fadd_rn(fmaxf(v, 0.f), 1.0e-6f))));
+  const int lane = threadIdx.x & 31, j = lane & 7;
+  for (int n0 = 0; n0 < p.N; n0 += NT / 8) {
+    const int n = n0 + (threadIdx.x >> 3);
+    const bool ok = n < p.N;
+    const float* c = p.centroid + (((int64_t)b * p.N + (ok ? n : 0)) * p.H + h) * HD;
+    float rv = 0.f, rm = 0.f;
+#pragma unroll
+    for (int i = 0; i < HD; i += 8) {
+      const float ci = c[i + j];
+      const float tv = __fmul_rn(__fmul_rn(ci, ci), s_var[i + j]);
+      rv = i == 0 ? tv : __fadd_rn(rv, tv);
+      if (!INT8) {
+        const float tm = __fmul_rn(ci, s_mean[i + j]);
+        rm = i == 0 ? tm : __fadd_rn(rm, tm);
+      }
     }
-    p.thr[((int64_t)b * p.N + n) * p.H + h] = t;
+#pragma unroll
+    for (int off = 1; off < 8; off <<= 1) {
+      rv = __fadd_rn(rv, __shfl_xor_sync(0xffffffffu, rv, off));
+      if (!INT8) rm = __fadd_rn(rm, __shfl_xor_sync(0xffffffffu, rm, off));
+    }
+    if (ok && j == 0) {
+      const float v = __fmul_rn(rv, s2sq);
+      float t;
+      if (INT8) {
+        t = __fmul_rn(p.tau, __fsqrt_rn(__fadd_rn(v, 1.0e-6f)));
+      } else {
+        const float m = __fmul_rn(rm, p.s2);
+        t = __fadd_rn(m, __fmul_rn(p.tau, __fsqrt_rn(__fadd_rn(fmaxf(v, 0.f), 1.0e-6f))));
+      }
+      p.thr[((int64_t)b * p.N + n) * p.H + h] = t;
+    }
   }
 }
 
@@ -487,11 +575,11 @@ __global__ void __launch_bounds__(256) gather_rows_kernel(GatherParams p) {
 
 template <int HD>
 static void launch_pool_t(const PoolParams& p, bool vamax, bool qquant, cudaStream_t st) {
-  dim3 grid((p.H * (HD / 8) + 127) / 128, p.npad, p.B);
-  if (vamax && qquant) pool_kernel<HD, true, true><<<grid, 128, 0, st>>>(p);
-  else if (vamax) pool_kernel<HD, true, false><<<grid, 128, 0, st>>>(p);
-  else if (qquant) pool_kernel<HD, false, true><<<grid, 128, 0, st>>>(p);
-  else pool_kernel<HD, false, false><<<grid, 128, 0, st>>>(p);
+  dim3 grid((p.H * (HD / 8) + 63) / 64, p.npad, 3 * p.B);
+  if (vamax && qquant) pool_kernel<HD, true, true><<<grid, 64, 0, st>>>(p);
+  else if (vamax) pool_kernel<HD, true, false><<<grid, 64, 0, st>>>(p);
+  else if (qquant) pool_kernel<HD, false, true><<<grid, 64, 0, st>>>(p);
+  else pool_kernel<HD, false, false><<<grid, 64, 0, st>>>(p);
 }
 
 void launch_pool(const PoolParams& p, int hd, bool vamax, bool qquant, cudaStream_t st) {
@@ -502,11 +590,11 @@ void launch_pool(const PoolParams& p, int hd, bool vamax, bool qquant, cudaStrea
 void launch_moments(const MomentsParams& p, int hd, bool int8, cudaStream_t st) {
   const int grid = p.B * p.H;
   if (hd == 128) {
-    if (int8) moments_kernel<128, true><<<grid, 128, 0, st>>>(p);
-    else moments_kernel<128, false><<<grid, 128, 0, st>>>(p);
+    if (int8) moments_kernel<128, true><<<grid, 512, 0, st>>>(p);
+    else moments_kernel<128, false><<<grid, 512, 0, st>>>(p);
   } else {
-    if (int8) moments_kernel<64, true><<<grid, 64, 0, st>>>(p);
-    else moments_kernel<64, false><<<grid, 64, 0, st>>>(p);
+    if (int8) moments_kernel<64, true><<<grid, 512, 0, st>>>(p);
+    else moments_kernel<64, false><<<grid, 512, 0, st>>>(p);
   }
 }
 
