@@ -21,6 +21,9 @@ int32_t fail(int32_t code, const std::string& msg) {
 }
 
 int32_t cuda_fail(cudaError_t e, const char* what) {
+  // clear the runtime's last-error slot (a launch error stays there otherwise and the
+  // next call's launch check would report it again); faults of the context stay sticky
+  (void)cudaGetLastError();
   return fail(SOLB200_ERR_CUDA, std::string(what) + ": " + cudaGetErrorString(e));
 }
 
@@ -208,14 +211,11 @@ int32_t run(const Plan& P, const Call& c) {
 
   MomentsParams mp{};
   mp.kc = pp.kc;
-  mp.centroid = pp.centroid;
   mp.vamax = pp.vamax;
   mp.kmean = at<float>(c.ws, P, SOLB200_BUF_KMEAN);
   mp.kvar = at<float>(c.ws, P, SOLB200_BUF_KVAR);
   mp.vscale = c.int8 ? at<float>(c.ws, P, SOLB200_BUF_VSCALE) : nullptr;
-  mp.thr = at<float>(c.ws, P, SOLB200_BUF_THR);
   mp.B = (int)P.B; mp.H = (int)P.H; mp.N = P.N; mp.npad = P.npad;
-  mp.s2 = s2; mp.tau = c.tau;
   if (prep) launch_moments(mp, hd, c.int8, c.st);
 
   if (c.int8 && prep) {
@@ -235,13 +235,15 @@ int32_t run(const Plan& P, const Call& c) {
   RouteParams rp{};
   rp.kc = pp.kc;
   rp.centroid = pp.centroid;
-  rp.thr = mp.thr;
+  rp.kmean = mp.kmean;
+  rp.kvar = mp.kvar;
+  rp.thr = at<float>(c.ws, P, SOLB200_BUF_THR);
   rp.mask = at<uint32_t>(c.ws, P, SOLB200_BUF_MASK);
   rp.count = at<int>(c.ws, P, SOLB200_BUF_COUNT);
   rp.lists = c.lists;
   rp.stat = c.stat;
   rp.B = (int)P.B; rp.H = (int)P.H; rp.N = P.N; rp.npad = P.npad; rp.nw = P.nw;
-  rp.s2 = s2;
+  rp.s2 = s2; rp.tau = c.tau; rp.int8 = c.int8 ? 1 : 0;
   const int64_t lim = (int64_t)1 << 30;
   auto clampi = [&](int64_t x) { return (int)(x < -lim ? -lim : (x > lim ? lim : x)); };
   rp.sink_kv0 = clampi(c.sink_kv[0]); rp.sink_kv1 = clampi(c.sink_kv[1]);
@@ -429,6 +431,16 @@ int32_t solb200_gather_rows(const void* const* src, void* const* dst, int32_t nt
   launch_gather(gp, static_cast<cudaStream_t>(stream));
   const cudaError_t e = cudaGetLastError();
   return e == cudaSuccess ? SOLB200_OK : cuda_fail(e, "gather launch");
+}
+
+int32_t solb200_selftest_quotient(const float* x, const float* s, int64_t n, uint64_t* bad, void* stream) {
+  int32_t rc = check_device();
+  if (rc) return rc;
+  if (!x || !s || !bad || n < 0) return fail(SOLB200_ERR_INVALID, "null pointer or negative count");
+  if (n == 0) return SOLB200_OK;
+  launch_quotient_selftest(x, s, n, reinterpret_cast<unsigned long long*>(bad), static_cast<cudaStream_t>(stream));
+  const cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? SOLB200_OK : cuda_fail(e, "selftest launch");
 }
 
 int32_t solb200_copy_heads(void* device, void* host, int64_t batch, int64_t tokens, int64_t heads,

@@ -27,6 +27,34 @@ enum DeviceError : int {
   kErrWaitDrain = 16,    // exit path could not drain in-flight copies / MMAs
 };
 
+// Programmatic dependent launch. Every kernel of the path is launched with
+// programmaticStreamSerializationAllowed (launch_pdl), and its first statement is
+// pdl_begin(): griddepcontrol.wait returns once the preceding grid in the stream has
+// completed and its memory is visible (at once when there is no such grid), then
+// griddepcontrol.launch_dependents lets the next kernel's CTAs be scheduled while this
+// one runs; they in turn wait in their own pdl_begin(). Nothing is read or written
+// before the wait, so the overlap is the next launch's setup and CTA placement only.
+__device__ __forceinline__ void pdl_begin() {
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
+template <typename... Params, typename... Args>
+inline cudaError_t launch_pdl(void (*kern)(Params...), dim3 grid, dim3 block, size_t smem,
+                              cudaStream_t st, Args&&... args) {
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kern, static_cast<Args&&>(args)...);
+}
+
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
 }

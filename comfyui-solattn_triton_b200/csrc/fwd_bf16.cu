@@ -32,6 +32,7 @@ sol_fwd_bf16_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_const
                     const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_kc,
                     const __grid_constant__ CUtensorMap tm_vc, const __grid_constant__ CUtensorMap tm_o,
                     const FwdParams p) {
+  pdl_begin();
   static_assert(HD == 64 || HD == 128, "head_dim 64 or 128");
   static_assert(BLK == 64 || BLK == 128, "block 64 or 128");
   constexpr int NBOX = HD / 64;                 // 64-column (128-byte) boxes per row
@@ -268,8 +269,7 @@ static cudaError_t launch_t(const FwdMaps& m, const FwdParams& p, cudaStream_t s
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return e;
   const unsigned grid = (unsigned)((int64_t)p.B * p.H * p.N);
-  kern<<<grid, 192, smem, st>>>(m.q, m.k, m.v, m.kc, m.vc, m.o, p);
-  return cudaGetLastError();
+  return launch_pdl(kern, dim3(grid), dim3(192), smem, st, m.q, m.k, m.v, m.kc, m.vc, m.o, p);
 }
 
 cudaError_t launch_fwd_bf16(int hd, int blk, const FwdMaps& m, const FwdParams& p, cudaStream_t st) {

@@ -181,6 +181,14 @@ __device__ __forceinline__ float2 add2(float2 a, float2 b) {
   return *reinterpret_cast<float2*>(&r);
 }
 
+__device__ __forceinline__ float2 mul2(float2 a, float2 b) {
+  uint64_t r;
+  asm("mul.f32x2 %0, %1, %2;"
+      : "=l"(r)
+      : "l"(*reinterpret_cast<uint64_t*>(&a)), "l"(*reinterpret_cast<uint64_t*>(&b)));
+  return *reinterpret_cast<float2*>(&r);
+}
+
 __device__ __forceinline__ float max3(float a, float b, float c) {
   float r;
   asm("max.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));

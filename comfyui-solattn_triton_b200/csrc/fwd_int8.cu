@@ -38,6 +38,7 @@ sol_fwd_int8_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_const
                     const __grid_constant__ CUtensorMap tm_qi, const __grid_constant__ CUtensorMap tm_ki,
                     const __grid_constant__ CUtensorMap tm_vi, const __grid_constant__ CUtensorMap tm_v,
                     const FwdParams p) {
+  pdl_begin();
   constexpr int NBOX = HD / 64;
   constexpr uint32_t BOX = 128 * 128;
   constexpr int RB = HD;                    // bytes per int8 q/k/v row
@@ -441,8 +442,7 @@ static cudaError_t launch_t(const FwdMaps& m, const FwdParams& p, cudaStream_t s
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return e;
   const unsigned grid = (unsigned)((int64_t)p.B * p.H * p.N);
-  kern<<<grid, 192, smem, st>>>(m.q, m.kc, m.vc, m.o, m.qi, m.ki, m.vi, m.v, p);
-  return cudaGetLastError();
+  return launch_pdl(kern, dim3(grid), dim3(192), smem, st, m.q, m.kc, m.vc, m.o, m.qi, m.ki, m.vi, m.v, p);
 }
 
 cudaError_t launch_fwd_int8(int hd, int blk, const FwdMaps& m, const FwdParams& p, cudaStream_t st) {

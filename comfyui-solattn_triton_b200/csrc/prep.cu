@@ -2,8 +2,9 @@
 //   pool_kernel      one pass over Q, K, V: kc (block mean of K), vc (block sum of V),
 //                    q-block centroids, optional per-block |V| max and per-token Q int8
 //   moments_kernel   per (b, h): kc mean/variance (INT8: k_mean, kc centred in place,
-//                    V scales) and the per-q-block routing threshold
-//   route_kernel     exact-block bitmask [B,H,N,NW], counts, optional index lists
+//                    V scales)
+//   route_kernel     per-q-block routing threshold, exact-block bitmask [B,H,N,NW],
+//                    counts, optional index lists
 //   quant_kv_kernel  per-token int8 of K - k_mean, per-channel int8 of V
 //   morton kernels   Z-order ranks (no sort) and a row gather for the reorder
 //
@@ -37,21 +38,63 @@ __device__ __forceinline__ uint4 pack8_bf16(const float (&x)[8]) {
   return u;
 }
 
-// round half away from zero of an already clamped value, as trunc(x +- 0.5)
-__device__ __forceinline__ int round_half_away(float x) {
-  return x >= 0.f ? __float2int_rz(__fadd_rn(x, 0.5f)) : __float2int_rz(__fsub_rn(x, 0.5f));
+// RN(x / s) for s > 0 from y = RN(1/s) (__frcp_rn, computed once per scale) without a
+// division per element, by Markstein's theorem (Markstein 1990; Muller et al.,
+// Handbook of Floating-Point Arithmetic, section on FMA-based division): if y is within
+// half an ulp of 1/s, q within one ulp of x/s and r = x - s*q exact (an FMA), then
+// RN(q + r*y) = RN(x/s). q0 = RN(x*y) can be 1.5 ulp off, so one correction first
+// brings it within half an ulp (plus a rounding of its remainder), then the second
+// is the theorem's step. Exact while the remainders are normal numbers, which holds
+// for every quotient the int8 codes depend on (|x/s| >= 2^-2 with s >= 1e-8); tiny
+// quotients may differ in the last place and still round to the code 0.
+__device__ __forceinline__ float quotient_rn(float x, float s, float y) {
+  const float q0 = __fmul_rn(x, y);
+  const float q1 = __fmaf_rn(__fmaf_rn(-s, q0, x), y, q0);
+  return __fmaf_rn(__fmaf_rn(-s, q1, x), y, q1);
+}
+
+// The int8 code of q: round half away from zero as sign(q) * trunc(RN(|q| + 0.5)) (x + 0.5
+// rounded, then truncated: the arithmetic of the reference's conversion), clamped to
+// +-127; returned in the low byte (two's complement). Clamping |q| to 127 first gives
+// the same code whether the reference clamps before rounding (_fused_prep.py) or after
+// (_fused_quant.py): rounding is monotonic and maps 127 to 127. trunc(w), w in
+// [0.5, 127.5], is read from the bits of w + 2^23 added with rounding toward zero (an
+// FMA-pipe add instead of the conversion unit); the sign is applied as (m ^ s) - s.
+__device__ __forceinline__ uint32_t code_byte(float q) {
+  const float w = __fadd_rn(fminf(fabsf(q), 127.f), 0.5f);
+  const uint32_t m = __float_as_uint(__fadd_rz(w, 8388608.f));   // 2^23 + trunc(w)
+  const uint32_t sgn = (uint32_t)((int32_t)__float_as_uint(q) >> 31);
+  return (m ^ sgn) - sgn;
+}
+
+// eight int8 codes (low bytes of c[0..7]) packed into two words, c[0] lowest
+__device__ __forceinline__ uint2 pack_codes(const uint32_t (&c)[8]) {
+  uint32_t a, b, lo, hi;
+  asm("prmt.b32 %0, %1, %2, 0x0040;" : "=r"(a) : "r"(c[0]), "r"(c[1]));
+  asm("prmt.b32 %0, %1, %2, 0x0040;" : "=r"(b) : "r"(c[2]), "r"(c[3]));
+  asm("prmt.b32 %0, %1, %2, 0x5410;" : "=r"(lo) : "r"(a), "r"(b));
+  asm("prmt.b32 %0, %1, %2, 0x0040;" : "=r"(a) : "r"(c[4]), "r"(c[5]));
+  asm("prmt.b32 %0, %1, %2, 0x0040;" : "=r"(b) : "r"(c[6]), "r"(c[7]));
+  asm("prmt.b32 %0, %1, %2, 0x5410;" : "=r"(hi) : "r"(a), "r"(b));
+  return make_uint2(lo, hi);
 }
 
 // One thread owns 8 consecutive channels (16 bytes) of one head and one of the three
 // tensors (role 0: Q -> centroid and, for INT8, qi / qs; role 1: K -> kc; role 2:
 // V -> vc and |V| max), so a call with few heads still has three threads per channel
 // group in flight. Rows are accumulated in token order (row 0 first) in fp32, the
-// order of the reference's block sums. Grid: (ceil(H*D/8 / 64), Npad, 3*B); 64 threads.
+// order of the reference's block sums; the loads of ROWS rows are issued before any of
+// them is added, so a thread keeps ROWS x 16 bytes in flight.
+// Grid: (3*ceil(H*D/8 / NT), Npad, B), role = blockIdx.x % 3 so that the three roles (the
+// Q role carries the INT8 quantisation) interleave in launch order; NT = 32 or 64
+// threads (launch_pool_t).
 template <int HD, bool VAMAX, bool QQUANT>
 __global__ void __launch_bounds__(64) pool_kernel(PoolParams p) {
+  pdl_begin();
   constexpr int LANES_PER_HEAD = HD / 8;
-  const int g = blockIdx.x * 64 + threadIdx.x;
-  const int n = blockIdx.y, b = blockIdx.z / 3, role = blockIdx.z % 3;
+  constexpr int ROWS = (VAMAX || QQUANT) ? 8 : 16;   // the INT8 variants keep fewer rows in registers
+  const int g = (blockIdx.x / 3) * blockDim.x + threadIdx.x;
+  const int n = blockIdx.y, role = blockIdx.x % 3, b = blockIdx.z;
   const bool active = g < p.H * LANES_PER_HEAD;
   const int h = g / LANES_PER_HEAD;
   const int d0 = (g % LANES_PER_HEAD) * 8;
@@ -78,43 +121,53 @@ __global__ void __launch_bounds__(64) pool_kernel(PoolParams p) {
   float sum[8], vmax[8];
 #pragma unroll
   for (int i = 0; i < 8; ++i) sum[i] = vmax[i] = 0.f;
-#pragma unroll 8
-  for (int r = r0; r < r1; ++r) {
-    float x[8];
-    if (active) {
-      load8(src + (int64_t)r * st, x);
-    } else {
+  for (int rb = r0; rb < r1; rb += ROWS) {
+    uint4 u[ROWS];
 #pragma unroll
-      for (int i = 0; i < 8; ++i) x[i] = 0.f;
-    }
+    for (int j = 0; j < ROWS; ++j)
+      u[j] = (active && rb + j < r1)
+                 ? __ldg(reinterpret_cast<const uint4*>(src + (int64_t)(rb + j) * st))
+                 : make_uint4(0, 0, 0, 0);
 #pragma unroll
-    for (int i = 0; i < 8; ++i) sum[i] = __fadd_rn(sum[i], x[i]);
-    if (VAMAX && role == 2) {
+    for (int j = 0; j < ROWS; ++j) {
+      const int r = rb + j;
+      if (r >= r1) break;   // uniform over the CTA
+      float x[8];
+      {
+        const __nv_bfloat162* hx = reinterpret_cast<const __nv_bfloat162*>(&u[j]);
 #pragma unroll
-      for (int i = 0; i < 8; ++i) vmax[i] = fmaxf(vmax[i], fabsf(x[i]));
-    }
-    if (QQUANT && role == 0) {
-      // per-token symmetric int8 of Q (_fused_prep.py:36-44): s = max|x| / 127,
-      // floor at 1e-8, clamp(x / s, +-127), round half away from zero.
-      float amax = 0.f;
-#pragma unroll
-      for (int i = 0; i < 8; ++i) amax = fmaxf(amax, fabsf(x[i]));
-#pragma unroll
-      for (int off = 1; off < LANES_PER_HEAD; off <<= 1)
-        amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, off));
-      const float s = __fdiv_rn(amax, 127.f);
-      const float s_safe = s > 1e-8f ? s : 1e-8f;
-      if (active) {
-        uint32_t lo = 0, hi = 0;
-#pragma unroll
-        for (int i = 0; i < 8; ++i) {
-          float xv = fminf(fmaxf(__fdiv_rn(x[i], s_safe), -127.f), 127.f);
-          const uint32_t byte = (uint32_t)(round_half_away(xv) & 0xff);
-          if (i < 4) lo |= byte << (8 * i); else hi |= byte << (8 * (i - 4));
+        for (int i = 0; i < 4; ++i) {
+          const float2 f = __bfloat1622float2(hx[i]);
+          x[2 * i] = f.x;
+          x[2 * i + 1] = f.y;
         }
-        const int64_t qo = (((int64_t)b * p.T + r) * p.H + h) * HD + d0;
-        *reinterpret_cast<uint2*>(p.qi + qo) = make_uint2(lo, hi);
-        if (d0 == 0) p.qs[((int64_t)b * p.H + h) * p.tp + r] = s_safe;
+      }
+#pragma unroll
+      for (int i = 0; i < 8; ++i) sum[i] = __fadd_rn(sum[i], x[i]);
+      if (VAMAX && role == 2) {
+#pragma unroll
+        for (int i = 0; i < 8; ++i) vmax[i] = fmaxf(vmax[i], fabsf(x[i]));
+      }
+      if (QQUANT && role == 0) {
+        // per-token symmetric int8 of Q (_fused_prep.py:36-44): s = max|x| / 127,
+        // floor at 1e-8, clamp(x / s, +-127), round half away from zero.
+        float amax = 0.f;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) amax = fmaxf(amax, fabsf(x[i]));
+#pragma unroll
+        for (int off = 1; off < LANES_PER_HEAD; off <<= 1)
+          amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, off));
+        const float s = __fdiv_rn(amax, 127.f);
+        const float s_safe = s > 1e-8f ? s : 1e-8f;
+        const float y = __frcp_rn(s_safe);
+        if (active) {
+          uint32_t c[8];
+#pragma unroll
+          for (int i = 0; i < 8; ++i) c[i] = code_byte(quotient_rn(x[i], s_safe, y));
+          const int64_t qo = (((int64_t)b * p.T + r) * p.H + h) * HD + d0;
+          *reinterpret_cast<uint2*>(p.qi + qo) = pack_codes(c);
+          if (d0 == 0) p.qs[((int64_t)b * p.H + h) * p.tp + r] = s_safe;
+        }
       }
     }
   }
@@ -236,101 +289,79 @@ __device__ void cascade_sum_par(int count, F x, float* s_chunk /* [64][HD] */, f
   __syncthreads();
 }
 
-// One CTA per (b, h), 512 threads.
-// BF16 mode (_preprocess.py:240-243, 149-164): kcm = mean_n kc, kcv = mean_n (kc-kcm)^2,
-//   thr = (c.kcm)*s2 + tau*sqrt(max((c^2.kcv)*s2^2, 0) + 1e-6).
-// INT8 mode (_fused_prep.py:77-81, 50-59; _fused_quant.py:103): k_mean = mean_n kc,
-//   kc <- bf16(kc - k_mean), kcv = mean_n kc^2, vscale = max(amax/127, 1e-8),
-//   thr = tau*sqrt((c^2.kcv)*s2^2 + 1e-6).
-// The D-sums of the threshold follow numpy's 8-way pairwise order: lane j of an 8-lane
-// group runs partial sum j, and three xor shuffles combine them as
-// ((r0+r1)+(r2+r3))+((r4+r5)+(r6+r7)).
-template <int HD, bool INT8>
-__global__ void __launch_bounds__(512) moments_kernel(MomentsParams p) {
-  constexpr int NT = 512;
-  __shared__ float s_chunk[64 * HD];
-  __shared__ float s_mean[HD], s_var[HD];
-  const int bh = blockIdx.x;
+// One CTA per (b, h, 16-channel slab), 256 threads. The slab's kc values (N x 16 bf16)
+// are staged in shared memory once and both cascade passes read them there (STAGED;
+// slabs too large for shared memory read them from global memory).
+// BF16 mode (_preprocess.py:240-243): kcm = mean_n kc, kcv = mean_n (kc-kcm)^2.
+// INT8 mode (_fused_prep.py:77-81; _fused_quant.py:103): k_mean = mean_n kc,
+//   kc <- bf16(kc - k_mean), kcv = mean_n kc^2, vscale = max(amax/127, 1e-8).
+// The per-q-block thresholds that use these moments are computed by route_kernel.
+constexpr int kMomentsCh = 16;
+constexpr int kMomentsThreads = 256;
+
+template <int HD, bool INT8, bool STAGED>
+__global__ void __launch_bounds__(kMomentsThreads) moments_kernel(MomentsParams p) {
+  pdl_begin();
+  constexpr int NT = kMomentsThreads, CH = kMomentsCh;
+  extern __shared__ __align__(16) __nv_bfloat16 s_x[];   // [N][CH] when STAGED
+  __shared__ float s_chunk[64 * CH];
+  __shared__ float s_mean[CH], s_var[CH];
+  const int bh = blockIdx.x, c0 = blockIdx.y * CH;
   const int b = bh / p.H, h = bh % p.H;
   const int64_t row = (int64_t)p.H * HD;
-  __nv_bfloat16* kc0 = p.kc + ((int64_t)b * p.npad) * row + (int64_t)h * HD;
-  auto kc_at = [&](int n, int d) { return __bfloat162float(kc0[(int64_t)n * row + d]); };
-  const float inv_n = (float)p.N;
-  cascade_sum_par<HD, NT>(p.N, kc_at, s_chunk, s_mean);
-  if (threadIdx.x < HD) s_mean[threadIdx.x] = __fdiv_rn(s_mean[threadIdx.x], inv_n);
-  __syncthreads();
-  if (INT8) {
-    for (int it = threadIdx.x; it < p.N * HD; it += NT) {
-      const int n = it / HD, d = it % HD;
-      kc0[(int64_t)n * row + d] = __float2bfloat16_rn(__fsub_rn(kc_at(n, d), s_mean[d]));
+  __nv_bfloat16* kc0 = p.kc + ((int64_t)b * p.npad) * row + (int64_t)h * HD + c0;
+  if (STAGED) {
+    for (int i = threadIdx.x; i < p.N * (CH / 8); i += NT) {
+      const int n = i / (CH / 8), part = i % (CH / 8);
+      *reinterpret_cast<uint4*>(s_x + n * CH + part * 8) =
+          __ldg(reinterpret_cast<const uint4*>(kc0 + (int64_t)n * row + part * 8));
     }
     __syncthreads();
-    cascade_sum_par<HD, NT>(p.N, [&](int n, int d) {
+  }
+  auto kc_at = [&](int n, int d) {
+    return __bfloat162float(STAGED ? s_x[n * CH + d] : kc0[(int64_t)n * row + d]);
+  };
+  cascade_sum_par<CH, NT>(p.N, kc_at, s_chunk, s_mean);
+  if (threadIdx.x < CH) s_mean[threadIdx.x] = __fdiv_rn(s_mean[threadIdx.x], (float)p.N);
+  __syncthreads();
+  if (INT8) {
+    for (int i = threadIdx.x; i < p.N * CH; i += NT) {
+      const int n = i / CH, d = i % CH;
+      const __nv_bfloat16 cb = __float2bfloat16_rn(__fsub_rn(kc_at(n, d), s_mean[d]));
+      kc0[(int64_t)n * row + d] = cb;
+      if (STAGED) s_x[n * CH + d] = cb;
+    }
+    __syncthreads();
+    cascade_sum_par<CH, NT>(p.N, [&](int n, int d) {
       const float x = kc_at(n, d);
       return __fmul_rn(x, x);
     }, s_chunk, s_var);
     if (p.vamax) {
       // |V| max over the blocks: order-free, partial maxima over row strips
       float* s_max = s_chunk;
-      constexpr int STRIPS = NT / HD;
-      const int d = threadIdx.x % HD, strip = threadIdx.x / HD;
-      const float* vam = p.vamax + ((int64_t)b * p.N) * row + (int64_t)h * HD + d;
+      constexpr int STRIPS = NT / CH;
+      const int d = threadIdx.x % CH, strip = threadIdx.x / CH;
+      const float* vam = p.vamax + ((int64_t)b * p.N) * row + (int64_t)h * HD + c0 + d;
       float amax = 0.f;
-      for (int n = strip; n < p.N; n += STRIPS) amax = fmaxf(amax, vam[(int64_t)n * row]);
-      s_max[strip * HD + d] = amax;
+#pragma unroll 4
+      for (int n = strip; n < p.N; n += STRIPS) amax = fmaxf(amax, __ldg(vam + (int64_t)n * row));
+      s_max[strip * CH + d] = amax;
       __syncthreads();
-      if (threadIdx.x < HD) {
+      if (threadIdx.x < CH) {
         float m = 0.f;
-        for (int k = 0; k < STRIPS; ++k) m = fmaxf(m, s_max[k * HD + threadIdx.x]);
-        p.vscale[(int64_t)bh * HD + threadIdx.x] = fmaxf(__fdiv_rn(m, 127.f), 1e-8f);
+        for (int k = 0; k < STRIPS; ++k) m = fmaxf(m, s_max[k * CH + threadIdx.x]);
+        p.vscale[(int64_t)bh * HD + c0 + threadIdx.x] = fmaxf(__fdiv_rn(m, 127.f), 1e-8f);
       }
     }
   } else {
-    cascade_sum_par<HD, NT>(p.N, [&](int n, int d) {
+    cascade_sum_par<CH, NT>(p.N, [&](int n, int d) {
       const float x = __fsub_rn(kc_at(n, d), s_mean[d]);
       return __fmul_rn(x, x);
     }, s_chunk, s_var);
   }
-  if (threadIdx.x < HD) {
-    s_var[threadIdx.x] = __fdiv_rn(s_var[threadIdx.x], inv_n);
-    p.kmean[(int64_t)bh * HD + threadIdx.x] = s_mean[threadIdx.x];
-    p.kvar[(int64_t)bh * HD + threadIdx.x] = s_var[threadIdx.x];
-  }
-  __syncthreads();
-  // thresholds: 8 lanes per query block, 4 blocks per warp, 64 per pass of the CTA
-  const float s2sq = __fmul_rn(p.s2, p.s2);
-  const int lane = threadIdx.x & 31, j = lane & 7;
-  for (int n0 = 0; n0 < p.N; n0 += NT / 8) {
-    const int n = n0 + (threadIdx.x >> 3);
-    const bool ok = n < p.N;
-    const float* c = p.centroid + (((int64_t)b * p.N + (ok ? n : 0)) * p.H + h) * HD;
-    float rv = 0.f, rm = 0.f;
-#pragma unroll
-    for (int i = 0; i < HD; i += 8) {
-      const float ci = c[i + j];
-      const float tv = __fmul_rn(__fmul_rn(ci, ci), s_var[i + j]);
-      rv = i == 0 ? tv : __fadd_rn(rv, tv);
-      if (!INT8) {
-        const float tm = __fmul_rn(ci, s_mean[i + j]);
-        rm = i == 0 ? tm : __fadd_rn(rm, tm);
-      }
-    }
-#pragma unroll
-    for (int off = 1; off < 8; off <<= 1) {
-      rv = __fadd_rn(rv, __shfl_xor_sync(0xffffffffu, rv, off));
-      if (!INT8) rm = __fadd_rn(rm, __shfl_xor_sync(0xffffffffu, rm, off));
-    }
-    if (ok && j == 0) {
-      const float v = __fmul_rn(rv, s2sq);
-      float t;
-      if (INT8) {
-        t = __fmul_rn(p.tau, __fsqrt_rn(__fadd_rn(v, 1.0e-6f)));
-      } else {
-        const float m = __fmul_rn(rm, p.s2);
-        t = __fadd_rn(m, __fmul_rn(p.tau, __fsqrt_rn(__fadd_rn(fmaxf(v, 0.f), 1.0e-6f))));
-      }
-      p.thr[((int64_t)b * p.N + n) * p.H + h] = t;
-    }
+  if (threadIdx.x < CH) {
+    p.kmean[(int64_t)bh * HD + c0 + threadIdx.x] = s_mean[threadIdx.x];
+    p.kvar[(int64_t)bh * HD + c0 + threadIdx.x] = __fdiv_rn(s_var[threadIdx.x], (float)p.N);
   }
 }
 
@@ -340,74 +371,176 @@ __global__ void __launch_bounds__(512) moments_kernel(MomentsParams p) {
 // Block j is exact for q-block n when (c_n . kc_j) * s2 > thr_n (the block-mean
 // score of _tri_fwd.py:279-286, with the row mean taken before the dot), or
 // |n - j| <= 1, or j is a sink KV block; a q-block inside the sink query range
-// attends every valid block exactly. One warp per q-block, lane = block within a
-// 32-block word. Grid: (ceil(N/8), B*H); 256 threads.
+// attends every valid block exactly.
+//
+// A CTA scores QB = 8 q-blocks against every key block of one (b, h). The key rows are
+// staged in shared memory a chunk of 8 words (256 rows) at a time with coalesced 16-byte
+// cp.async copies (the first chunk's are issued before anything else), rows padded to
+// kRowStride bytes so that lane l reading row l is free of bank conflicts. Warp w scores
+// word w of the chunk: lane l holds key row 32w + l in registers and scores it against
+// the 8 centroids (broadcast from shared memory) with packed f32x2 FMAs. Each score is
+// four interleaved partial sums over the channels d = 0, 1, 2, 3 (mod 4), in channel
+// order, added as (a0 + a1) + (a2 + a3). Grid: (ceil(N/8), B*H); 256 threads.
+//
+// The threshold of each q-block is computed here from its centroid:
+//   BF16 (_preprocess.py:149-164): thr = (c.kcm)*s2 + tau*sqrt(max((c^2.kcv)*s2^2, 0) + 1e-6)
+//   INT8 (_fused_prep.py:50-59):   thr = tau*sqrt((c^2.kcv)*s2^2 + 1e-6)
+// with the D-sums in numpy's 8-way pairwise order: lane j of each 8-lane group runs
+// partial sum j, and three xor shuffles combine them as ((r0+r1)+(r2+r3))+((r4+r5)+(r6+r7)).
+constexpr int kRouteQB = 8;
+constexpr int kRouteChunkWords = 8;   // one word per warp per chunk
+
+template <int HD>
+constexpr int route_row_stride() { return HD * 2 + 16; }
+
+template <int HD>
+constexpr size_t route_smem_bytes() { return (size_t)kRouteChunkWords * 32 * route_row_stride<HD>(); }
+
+__device__ __forceinline__ void cp_async16(uint32_t smem_addr, const void* gmem) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_addr), "l"(gmem) : "memory");
+}
+
 template <int HD>
 __global__ void __launch_bounds__(256) route_kernel(RouteParams p) {
-  constexpr int KPAD = HD + 2;   // bf16 row stride: consecutive rows shift one bank
-  __shared__ float s_c[8][HD];
-  __shared__ __align__(16) __nv_bfloat16 s_kc[32][KPAD];
-  __shared__ uint32_t s_words[8][64];
+  pdl_begin();
+  constexpr int QB = kRouteQB;
+  constexpr int KCH = HD / 8;                       // 16-byte chunks of a kc row
+  constexpr int RS = route_row_stride<HD>();        // staged row stride, bytes
+  extern __shared__ __align__(16) uint8_t s_rows[];  // [256][RS]
+  __shared__ __align__(16) float s_c[QB][HD];
+  __shared__ float s_km[HD], s_kv[HD];
+  __shared__ float s_thr[QB];
+  __shared__ uint32_t s_words[QB][64];
   const int bh = blockIdx.y;
   const int b = bh / p.H, h = bh % p.H;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int n = blockIdx.x * 8 + warp;
-  const bool row_ok = n < p.N;
-  for (int i = threadIdx.x; i < 8 * HD; i += 256) {
-    const int w = i / HD, d = i % HD, nn = blockIdx.x * 8 + w;
+  const int nbase = blockIdx.x * QB;
+  const int64_t krow = (int64_t)p.H * HD;
+  const __nv_bfloat16* kc0 = p.kc + (int64_t)b * p.npad * krow + (int64_t)h * HD;
+  const uint32_t rows_addr = smem_u32(s_rows);
+  // rows j < 32 * nw <= npad lie inside the zero-padded kc buffer
+  auto stage = [&](int w0, int cw) {
+    for (int i = threadIdx.x; i < cw * 32 * KCH; i += 256) {
+      const int r = i / KCH, c = i % KCH;
+      cp_async16(rows_addr + r * RS + c * 16, kc0 + (int64_t)(w0 * 32 + r) * krow + c * 8);
+    }
+    asm volatile("cp.async.commit_group;" ::: "memory");
+  };
+  stage(0, min(kRouteChunkWords, p.nw));
+  for (int i = threadIdx.x; i < QB * HD; i += 256) {
+    const int w = i / HD, d = i % HD, nn = nbase + w;
     s_c[w][d] = nn < p.N ? p.centroid[(((int64_t)b * p.N + nn) * p.H + h) * HD + d] : 0.f;
   }
-  const float thr = row_ok ? p.thr[((int64_t)b * p.N + n) * p.H + h] : 0.f;
-  const bool q_sink = n >= p.sink_q0 && n < p.sink_q1;
-  int total = 0;
-  for (int jw = 0; jw < p.nw; ++jw) {
-    __syncthreads();
-    for (int i = threadIdx.x; i < 32 * (HD / 8); i += 256) {
-      const int r = i / (HD / 8), c8 = (i % (HD / 8)) * 8;
-      const int j = jw * 32 + r;
-      uint4 u = make_uint4(0, 0, 0, 0);
-      if (j < p.N)
-        u = __ldg(reinterpret_cast<const uint4*>(
-            p.kc + (((int64_t)b * p.npad + j) * p.H + h) * HD + c8));
-      uint32_t* dst = reinterpret_cast<uint32_t*>(&s_kc[r][c8]);
-      dst[0] = u.x; dst[1] = u.y; dst[2] = u.z; dst[3] = u.w;
-    }
-    __syncthreads();
-    const int j = jw * 32 + lane;
-    float acc = 0.f;
-    const __nv_bfloat162* kr = reinterpret_cast<const __nv_bfloat162*>(&s_kc[lane][0]);
-#pragma unroll 16
-    for (int d2 = 0; d2 < HD / 2; ++d2) {
-      const float2 kv = __bfloat1622float2(kr[d2]);
-      acc = fmaf(s_c[warp][2 * d2], kv.x, acc);
-      acc = fmaf(s_c[warp][2 * d2 + 1], kv.y, acc);
-    }
-    const float score = __fmul_rn(acc, p.s2);
-    const bool valid = j < p.N;
-    bool exact = (score > thr) || (abs(n - j) <= 1) || (j >= p.sink_kv0 && j < p.sink_kv1);
-    if (q_sink) exact = true;
-    exact = exact && valid;
-    const uint32_t word = __ballot_sync(0xffffffffu, exact);
-    if (row_ok) {
-      if (lane == 0) {
-        p.mask[(((int64_t)b * p.H + h) * p.N + n) * p.nw + jw] = word;
-        if (jw < 64) s_words[warp][jw] = word;
+  for (int d = threadIdx.x; d < HD; d += 256) {
+    s_km[d] = p.kmean[(int64_t)bh * HD + d];
+    s_kv[d] = p.kvar[(int64_t)bh * HD + d];
+  }
+  __syncthreads();
+  {
+    const int n = nbase + warp;
+    const int j8 = lane & 7;
+    float rv = 0.f, rm = 0.f;
+#pragma unroll
+    for (int i = 0; i < HD; i += 8) {
+      const float ci = s_c[warp][i + j8];
+      const float tv = __fmul_rn(__fmul_rn(ci, ci), s_kv[i + j8]);
+      rv = i == 0 ? tv : __fadd_rn(rv, tv);
+      if (!p.int8) {
+        const float tm = __fmul_rn(ci, s_km[i + j8]);
+        rm = i == 0 ? tm : __fadd_rn(rm, tm);
       }
-      if (p.stat && valid) p.stat[(((int64_t)b * p.H + h) * p.N + n) * p.N + j] = score;
-      total += __popc(word);
+    }
+#pragma unroll
+    for (int off = 1; off < 8; off <<= 1) {
+      rv = __fadd_rn(rv, __shfl_xor_sync(0xffffffffu, rv, off));
+      rm = __fadd_rn(rm, __shfl_xor_sync(0xffffffffu, rm, off));
+    }
+    const float v = __fmul_rn(rv, __fmul_rn(p.s2, p.s2));
+    float t;
+    if (p.int8) {
+      t = __fmul_rn(p.tau, __fsqrt_rn(__fadd_rn(v, 1.0e-6f)));
+    } else {
+      t = __fadd_rn(__fmul_rn(rm, p.s2),
+                    __fmul_rn(p.tau, __fsqrt_rn(__fadd_rn(fmaxf(v, 0.f), 1.0e-6f))));
+    }
+    if (lane == 0) {
+      s_thr[warp] = t;
+      if (n < p.N) p.thr[((int64_t)b * p.N + n) * p.H + h] = t;
     }
   }
-  if (!row_ok) return;
+  float thr[QB];
+  const float4* c4 = reinterpret_cast<const float4*>(&s_c[0][0]);
+  for (int w0 = 0; w0 < p.nw; w0 += kRouteChunkWords) {
+    const int cw = min(kRouteChunkWords, p.nw - w0);
+    asm volatile("cp.async.wait_all;" ::: "memory");
+    __syncthreads();   // the chunk (and, the first time, the thresholds) is visible
+    if (w0 == 0) {
+#pragma unroll
+      for (int q = 0; q < QB; ++q) thr[q] = s_thr[q];
+    }
+    if (warp < cw) {
+      const int jw = w0 + warp;
+      const int j = jw * 32 + lane;
+      const bool valid = j < p.N;
+      const uint4* kr = reinterpret_cast<const uint4*>(s_rows + (warp * 32 + lane) * RS);
+      float2 acc[QB][2];
+#pragma unroll
+      for (int q = 0; q < QB; ++q) acc[q][0] = acc[q][1] = make_float2(0.f, 0.f);
+#pragma unroll
+      for (int t = 0; t < KCH; ++t) {
+        // channels 8t .. 8t+7 of row j as (k0,k1) (k2,k3) (k4,k5) (k6,k7)
+        const uint4 kv4 = kr[t];
+        const float2 k01 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&kv4.x));
+        const float2 k23 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&kv4.y));
+        const float2 k45 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&kv4.z));
+        const float2 k67 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&kv4.w));
+#pragma unroll
+        for (int q = 0; q < QB; ++q) {
+          const float4 ca = c4[q * (HD / 4) + 2 * t], cb = c4[q * (HD / 4) + 2 * t + 1];
+          acc[q][0] = __ffma2_rn(make_float2(ca.x, ca.y), k01, acc[q][0]);
+          acc[q][1] = __ffma2_rn(make_float2(ca.z, ca.w), k23, acc[q][1]);
+          acc[q][0] = __ffma2_rn(make_float2(cb.x, cb.y), k45, acc[q][0]);
+          acc[q][1] = __ffma2_rn(make_float2(cb.z, cb.w), k67, acc[q][1]);
+        }
+      }
+      uint32_t mine = 0;
+#pragma unroll
+      for (int q = 0; q < QB; ++q) {
+        const int n = nbase + q;
+        const float score = __fmul_rn(__fadd_rn(__fadd_rn(acc[q][0].x, acc[q][0].y),
+                                                __fadd_rn(acc[q][1].x, acc[q][1].y)), p.s2);
+        bool exact = (score > thr[q]) || (abs(n - j) <= 1) || (j >= p.sink_kv0 && j < p.sink_kv1);
+        if (n >= p.sink_q0 && n < p.sink_q1) exact = true;
+        const uint32_t word = __ballot_sync(0xffffffffu, exact && valid);
+        if (lane == q) mine = word;
+        if (p.stat && valid && n < p.N) p.stat[(((int64_t)b * p.H + h) * p.N + n) * p.N + j] = score;
+      }
+      if (lane < QB && nbase + lane < p.N) {
+        p.mask[(((int64_t)b * p.H + h) * p.N + nbase + lane) * p.nw + jw] = mine;
+        if (jw < 64) s_words[lane][jw] = mine;
+      }
+    }
+    if (w0 + kRouteChunkWords < p.nw) {
+      __syncthreads();   // every warp is done with this chunk
+      stage(w0 + kRouteChunkWords, min(kRouteChunkWords, p.nw - w0 - kRouteChunkWords));
+    }
+  }
+  __syncthreads();   // every word of the CTA's q-blocks is in s_words / mask
+  const int n = nbase + warp;   // warps 0 .. QB-1 finish one q-block each
+  if (warp >= QB || n >= p.N) return;
   const int64_t urow = ((int64_t)b * p.H + h) * p.N + n;
+  auto word_at = [&](int w) { return w < 64 ? s_words[warp][w] : p.mask[urow * p.nw + w]; };
+  int total = 0;
+  for (int w = lane; w < p.nw; w += 32) total += __popc(word_at(w));
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) total += __shfl_xor_sync(0xffffffffu, total, off);
   if (lane == 0) p.count[urow] = total;
   if (p.lists) {
-    __syncwarp();
     int* out = p.lists + urow * p.N;
     int base = 0;
     for (int w0 = 0; w0 < p.nw; w0 += 32) {
       const int w = w0 + lane;
-      uint32_t bits = 0;
-      if (w < p.nw) bits = w < 64 ? s_words[warp][w] : p.mask[urow * p.nw + w];
+      uint32_t bits = w < p.nw ? word_at(w) : 0u;
       const int c = __popc(bits);
       int incl = c;
 #pragma unroll
@@ -433,57 +566,136 @@ __global__ void __launch_bounds__(256) route_kernel(RouteParams p) {
 // K: per-(token, head) int8 of K - k_mean (_fused_quant.py:8-42): s = max|x|/127,
 //    floor 1e-8, round half away from zero of x/s, clamp +-127.
 // V: per-channel int8 with the (b, h, d) scale (_fused_quant.py:61-88).
-// One thread per 8 channels of a (token, head); a head's lanes share a warp.
+// One thread per 8 channels of a (head, group of TOK consecutive tokens); a head's lanes
+// share a warp. The K and V rows of all TOK tokens are loaded before any is quantised.
+constexpr int kQuantTok = 2;
+
+// int8 codes clamp(round half away from zero of x / den, +-127); rcp = RN(1 / den)
+__device__ __forceinline__ uint2 quant8(const float (&x)[8], const float (&den)[8], const float (&rcp)[8]) {
+  uint32_t c[8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) c[i] = code_byte(quotient_rn(x[i], den[i], rcp[i]));
+  return pack_codes(c);
+}
+
+__device__ __forceinline__ void unpack8(const uint4& u, float (&x)[8]) {
+  const __nv_bfloat162* hx = reinterpret_cast<const __nv_bfloat162*>(&u);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const float2 f = __bfloat1622float2(hx[i]);
+    x[2 * i] = f.x;
+    x[2 * i + 1] = f.y;
+  }
+}
+
 template <int HD>
-__global__ void __launch_bounds__(256) quant_kv_kernel(QuantParams p) {
-  constexpr int LPH = HD / 8;
+__global__ void __launch_bounds__(256, 3) quant_kv_kernel(QuantParams p) {
+  pdl_begin();
+  constexpr int LPH = HD / 8, TOK = kQuantTok;
+  const int64_t per_grp = (int64_t)p.H * LPH;
+  const int64_t groups = (p.T + TOK - 1) / TOK;
   const int64_t gid = (int64_t)blockIdx.x * 256 + threadIdx.x;
-  const int64_t per_tok = (int64_t)p.H * LPH;
-  const int64_t total = (int64_t)p.B * p.T * per_tok;
-  const bool active = gid < total;
+  const bool active = gid < (int64_t)p.B * groups * per_grp;
   const int64_t g = active ? gid : 0;
-  const int b = (int)(g / ((int64_t)p.T * per_tok));
-  const int64_t rem = g - (int64_t)b * p.T * per_tok;
-  const int t = (int)(rem / per_tok);
-  const int hl = (int)(rem % per_tok);
+  const int b = (int)(g / (groups * per_grp));
+  const int64_t rem = g - (int64_t)b * groups * per_grp;
+  const int t0 = (int)(rem / per_grp) * TOK;
+  const int hl = (int)(rem % per_grp);
   const int h = hl / LPH, d0 = (hl % LPH) * 8;
-  float xk[8];
-  load8(p.k + (int64_t)b * p.sk_b + (int64_t)t * p.sk_t + (int64_t)h * p.sk_h + d0, xk);
-  const float* m = p.kmean + ((int64_t)b * p.H + h) * HD + d0;
-  float amax = 0.f;
+  const bool with_v = p.vi != nullptr;
+  uint4 uk[TOK], uv[TOK];
 #pragma unroll
-  for (int i = 0; i < 8; ++i) {
-    xk[i] = __fsub_rn(xk[i], m[i]);
-    amax = fmaxf(amax, fabsf(xk[i]));
+  for (int i = 0; i < TOK; ++i) {
+    const bool ok = active && t0 + i < p.T;
+    const int t = ok ? t0 + i : 0;
+    uk[i] = ok ? __ldg(reinterpret_cast<const uint4*>(p.k + (int64_t)b * p.sk_b + (int64_t)t * p.sk_t +
+                                                      (int64_t)h * p.sk_h + d0))
+               : make_uint4(0, 0, 0, 0);
+    uv[i] = ok && with_v ? __ldg(reinterpret_cast<const uint4*>(p.v + (int64_t)b * p.sv_b + (int64_t)t * p.sv_t +
+                                                               (int64_t)h * p.sv_h + d0))
+                         : make_uint4(0, 0, 0, 0);
   }
-#pragma unroll
-  for (int off = 1; off < LPH; off <<= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, off));
-  const float s = __fdiv_rn(amax, 127.f);
-  const float s_safe = s > 1e-8f ? s : 1e-8f;
-  const int64_t o = (((int64_t)b * p.T + t) * p.H + h) * HD + d0;
-  uint32_t lo = 0, hi = 0;
-#pragma unroll
-  for (int i = 0; i < 8; ++i) {
-    const int qv = max(-127, min(127, round_half_away(__fdiv_rn(xk[i], s_safe))));
-    const uint32_t byte = (uint32_t)(qv & 0xff);
-    if (i < 4) lo |= byte << (8 * i); else hi |= byte << (8 * (i - 4));
-  }
-  if (!active) return;
-  *reinterpret_cast<uint2*>(p.ki + o) = make_uint2(lo, hi);
-  if (d0 == 0) p.ks[((int64_t)b * p.H + h) * p.tp + t] = s_safe;
-  if (p.vi) {
-    float xv[8];
-    load8(p.v + (int64_t)b * p.sv_b + (int64_t)t * p.sv_t + (int64_t)h * p.sv_h + d0, xv);
-    const float* sc = p.vscale + ((int64_t)b * p.H + h) * HD + d0;
-    lo = hi = 0;
-#pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      const int qv = max(-127, min(127, round_half_away(__fdiv_rn(xv[i], sc[i]))));
-      const uint32_t byte = (uint32_t)(qv & 0xff);
-      if (i < 4) lo |= byte << (8 * i); else hi |= byte << (8 * (i - 4));
+  float m[8], sc[8];
+  {
+    const float4* mp = reinterpret_cast<const float4*>(p.kmean + ((int64_t)b * p.H + h) * HD + d0);
+    const float4 m0 = __ldg(mp), m1 = __ldg(mp + 1);
+    m[0] = m0.x; m[1] = m0.y; m[2] = m0.z; m[3] = m0.w; m[4] = m1.x; m[5] = m1.y; m[6] = m1.z; m[7] = m1.w;
+    if (with_v) {
+      const float4* sp = reinterpret_cast<const float4*>(p.vscale + ((int64_t)b * p.H + h) * HD + d0);
+      const float4 s0 = __ldg(sp), s1 = __ldg(sp + 1);
+      sc[0] = s0.x; sc[1] = s0.y; sc[2] = s0.z; sc[3] = s0.w; sc[4] = s1.x; sc[5] = s1.y; sc[6] = s1.z; sc[7] = s1.w;
     }
-    *reinterpret_cast<uint2*>(p.vi + o) = make_uint2(lo, hi);
   }
+  float sc_rcp[8];
+#pragma unroll
+  for (int c = 0; c < 8; ++c) sc_rcp[c] = with_v ? __frcp_rn(sc[c]) : 0.f;
+#pragma unroll
+  for (int i = 0; i < TOK; ++i) {
+    const int t = t0 + i;
+    const bool ok = active && t < p.T;
+    float xk[8], den[8];
+    unpack8(uk[i], xk);
+    float amax = 0.f;
+#pragma unroll
+    for (int c = 0; c < 8; ++c) {
+      xk[c] = __fsub_rn(xk[c], m[c]);
+      amax = fmaxf(amax, fabsf(xk[c]));
+    }
+#pragma unroll
+    for (int off = 1; off < LPH; off <<= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, off));
+    const float s = __fdiv_rn(amax, 127.f);
+    const float s_safe = s > 1e-8f ? s : 1e-8f;
+    const float y = __frcp_rn(s_safe);
+    float rcp[8];
+#pragma unroll
+    for (int c = 0; c < 8; ++c) {
+      den[c] = s_safe;
+      rcp[c] = y;
+    }
+    const uint2 qk = quant8(xk, den, rcp);
+    const int64_t o = (((int64_t)b * p.T + t) * p.H + h) * HD + d0;
+    if (ok) {
+      *reinterpret_cast<uint2*>(p.ki + o) = qk;
+      if (d0 == 0) p.ks[((int64_t)b * p.H + h) * p.tp + t] = s_safe;
+    }
+    if (with_v) {
+      float xv[8];
+      unpack8(uv[i], xv);
+      const uint2 qv = quant8(xv, sc, sc_rcp);
+      if (ok) *reinterpret_cast<uint2*>(p.vi + o) = qv;
+    }
+  }
+}
+
+// Self-test of quotient_rn and code_byte against CUDA's IEEE division and
+// conversion on caller-given (x, s) pairs: counts the pairs whose quotient differs in
+// value from __fdiv_rn(x, s) (bad[0]) and whose int8 code (clamp after rounding, as
+// quant8) differs (bad[1]).
+__global__ void __launch_bounds__(256) quotient_selftest_kernel(const float* __restrict__ x,
+                                                                const float* __restrict__ s, int64_t n,
+                                                                unsigned long long* bad) {
+  pdl_begin();
+  unsigned long long nq = 0, nc = 0;
+  for (int64_t i = (int64_t)blockIdx.x * 256 + threadIdx.x; i < n; i += (int64_t)gridDim.x * 256) {
+    const float xi = x[i], si = s[i];
+    const float want = __fdiv_rn(xi, si);
+    const float got = quotient_rn(xi, si, __frcp_rn(si));
+    if (!(got == want)) ++nq;
+    const float wc = fminf(fmaxf(want, -256.f), 256.f);
+    const int want_code = max(-127, min(127, wc >= 0.f ? __float2int_rz(__fadd_rn(wc, 0.5f))
+                                                       : __float2int_rz(__fsub_rn(wc, 0.5f))));
+    const int got_code = (int)(int8_t)(code_byte(got) & 0xffu);
+    if (got_code != want_code) ++nc;
+  }
+  if (nq) atomicAdd(bad, nq);
+  if (nc) atomicAdd(bad + 1, nc);
+}
+
+void launch_quotient_selftest(const float* x, const float* s, int64_t n, unsigned long long* bad,
+                              cudaStream_t st) {
+  int64_t blocks = (n + 255) / 256;
+  blocks = blocks < 1 ? 1 : (blocks > 4096 ? 4096 : blocks);
+  launch_pdl(quotient_selftest_kernel, dim3((unsigned)blocks), dim3(256), 0, st, x, s, n, bad);
 }
 
 // -------------------------------------------------------------------- Morton
@@ -526,6 +738,7 @@ __device__ int64_t morton_rank(const int64_t (&c)[3], const int64_t (&dim)[3], i
 // block-alignment rotation of _morton_h3.py:42-61 (0 for the plain permutation).
 __global__ void morton_kernel(int64_t frames, int64_t height, int64_t width, int curve,
                               int64_t roll, int64_t* perm, int64_t* inverse) {
+  pdl_begin();
   const int64_t T = frames * height * width;
   const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   if (i >= T) return;
@@ -557,6 +770,7 @@ __global__ void morton_kernel(int64_t frames, int64_t height, int64_t width, int
 // warp per destination row, 16-byte vectors (row_bytes % 16 == 0).
 
 __global__ void __launch_bounds__(256) gather_rows_kernel(GatherParams p) {
+  pdl_begin();
   const int64_t warp_id = ((int64_t)blockIdx.x * 256 + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
   if (warp_id >= p.batch * p.rows) return;
@@ -575,11 +789,14 @@ __global__ void __launch_bounds__(256) gather_rows_kernel(GatherParams p) {
 
 template <int HD>
 static void launch_pool_t(const PoolParams& p, bool vamax, bool qquant, cudaStream_t st) {
-  dim3 grid((p.H * (HD / 8) + 63) / 64, p.npad, 3 * p.B);
-  if (vamax && qquant) pool_kernel<HD, true, true><<<grid, 64, 0, st>>>(p);
-  else if (vamax) pool_kernel<HD, true, false><<<grid, 64, 0, st>>>(p);
-  else if (qquant) pool_kernel<HD, false, true><<<grid, 64, 0, st>>>(p);
-  else pool_kernel<HD, false, false><<<grid, 64, 0, st>>>(p);
+  // 64-thread CTAs when the channel groups fill them, else 32 (fewer idle lanes at small H)
+  const int lanes = p.H * (HD / 8);
+  const int nt = lanes % 64 == 0 ? 64 : 32;
+  dim3 grid(3 * ((lanes + nt - 1) / nt), p.npad, p.B);
+  if (vamax && qquant) launch_pdl(pool_kernel<HD, true, true>, grid, dim3(nt), 0, st, p);
+  else if (vamax) launch_pdl(pool_kernel<HD, true, false>, grid, dim3(nt), 0, st, p);
+  else if (qquant) launch_pdl(pool_kernel<HD, false, true>, grid, dim3(nt), 0, st, p);
+  else launch_pdl(pool_kernel<HD, false, false>, grid, dim3(nt), 0, st, p);
 }
 
 void launch_pool(const PoolParams& p, int hd, bool vamax, bool qquant, cudaStream_t st) {
@@ -587,14 +804,28 @@ void launch_pool(const PoolParams& p, int hd, bool vamax, bool qquant, cudaStrea
   else launch_pool_t<64>(p, vamax, qquant, st);
 }
 
-void launch_moments(const MomentsParams& p, int hd, bool int8, cudaStream_t st) {
-  const int grid = p.B * p.H;
-  if (hd == 128) {
-    if (int8) moments_kernel<128, true><<<grid, 512, 0, st>>>(p);
-    else moments_kernel<128, false><<<grid, 512, 0, st>>>(p);
+template <int HD, bool INT8>
+static void launch_moments_t(const MomentsParams& p, cudaStream_t st) {
+  constexpr int kMaxStaged = 200 * 1024;
+  const size_t staged = (size_t)p.N * kMomentsCh * sizeof(__nv_bfloat16);
+  const dim3 grid(p.B * p.H, HD / kMomentsCh);
+  if (staged <= kMaxStaged) {
+    if (staged > 48 * 1024)   // opt-in on the current device (the attribute is per device)
+      cudaFuncSetAttribute(moments_kernel<HD, INT8, true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           kMaxStaged);
+    launch_pdl(moments_kernel<HD, INT8, true>, grid, dim3(kMomentsThreads), staged, st, p);
   } else {
-    if (int8) moments_kernel<64, true><<<grid, 512, 0, st>>>(p);
-    else moments_kernel<64, false><<<grid, 512, 0, st>>>(p);
+    launch_pdl(moments_kernel<HD, INT8, false>, grid, dim3(kMomentsThreads), 0, st, p);
+  }
+}
+
+void launch_moments(const MomentsParams& p, int hd, bool int8, cudaStream_t st) {
+  if (hd == 128) {
+    if (int8) launch_moments_t<128, true>(p, st);
+    else launch_moments_t<128, false>(p, st);
+  } else {
+    if (int8) launch_moments_t<64, true>(p, st);
+    else launch_moments_t<64, false>(p, st);
   }
 }
 
@@ -605,6 +836,7 @@ void launch_moments(const MomentsParams& p, int hd, bool int8, cudaStream_t st) 
 // matter: every unit's output is independent of when it runs.
 __global__ void __launch_bounds__(256) order_kernel(const int* __restrict__ count, int* __restrict__ order,
                                                     int n) {
+  pdl_begin();
   constexpr int kBins = 1024;
   __shared__ int hist[kBins];
   __shared__ int warp_tot[8];
@@ -647,32 +879,40 @@ __global__ void __launch_bounds__(256) order_kernel(const int* __restrict__ coun
 }
 
 void launch_order(const int* count, int* order, int bh_count, int n, cudaStream_t st) {
-  order_kernel<<<bh_count, 256, 0, st>>>(count, order, n);
+  launch_pdl(order_kernel, dim3(bh_count), dim3(256), 0, st, count, order, n);
+}
+
+template <int HD>
+static void launch_route_t(const RouteParams& p, cudaStream_t st) {
+  constexpr size_t smem = route_smem_bytes<HD>();
+  if (smem > 48 * 1024)   // opt-in on the current device (the attribute is per device)
+    cudaFuncSetAttribute(route_kernel<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  const dim3 grid((p.N + kRouteQB - 1) / kRouteQB, p.B * p.H);
+  launch_pdl(route_kernel<HD>, grid, dim3(256), smem, st, p);
 }
 
 void launch_route(const RouteParams& p, int hd, cudaStream_t st) {
-  dim3 grid((p.N + 7) / 8, p.B * p.H);
-  if (hd == 128) route_kernel<128><<<grid, 256, 0, st>>>(p);
-  else route_kernel<64><<<grid, 256, 0, st>>>(p);
+  if (hd == 128) launch_route_t<128>(p, st);
+  else launch_route_t<64>(p, st);
 }
 
 void launch_quant_kv(const QuantParams& p, int hd, cudaStream_t st) {
-  const int64_t total = (int64_t)p.B * p.T * p.H * (hd / 8);
+  const int64_t total = (int64_t)p.B * ((p.T + kQuantTok - 1) / kQuantTok) * p.H * (hd / 8);
   const int64_t grid = (total + 255) / 256;
-  if (hd == 128) quant_kv_kernel<128><<<(unsigned)grid, 256, 0, st>>>(p);
-  else quant_kv_kernel<64><<<(unsigned)grid, 256, 0, st>>>(p);
+  if (hd == 128) launch_pdl(quant_kv_kernel<128>, dim3((unsigned)grid), dim3(256), 0, st, p);
+  else launch_pdl(quant_kv_kernel<64>, dim3((unsigned)grid), dim3(256), 0, st, p);
 }
 
 void launch_morton(int64_t frames, int64_t height, int64_t width, int curve, int64_t roll,
                    int64_t* perm, int64_t* inverse, cudaStream_t st) {
   const int64_t T = frames * height * width;
-  morton_kernel<<<(unsigned)((T + 255) / 256), 256, 0, st>>>(frames, height, width, curve, roll,
-                                                             perm, inverse);
+  launch_pdl(morton_kernel, dim3((unsigned)((T + 255) / 256)), dim3(256), 0, st, frames, height, width, curve,
+             roll, perm, inverse);
 }
 
 void launch_gather(const GatherParams& p, cudaStream_t st) {
   const int64_t warps = p.batch * p.rows;
-  gather_rows_kernel<<<(unsigned)((warps * 32 + 255) / 256), 256, 0, st>>>(p);
+  launch_pdl(gather_rows_kernel, dim3((unsigned)((warps * 32 + 255) / 256)), dim3(256), 0, st, p);
 }
 
 }  // namespace solb200

@@ -18,26 +18,26 @@ struct PoolParams {
 
 struct MomentsParams {
   __nv_bfloat16* kc;          // [B, Npad, H, D]; centred in place in INT8 mode
-  const float* centroid;      // [B, N, H, D]
   const float* vamax;         // [B, N, H, D] (INT8 mode)
   float* kmean;               // [B, H, D]
   float* kvar;                // [B, H, D]
   float* vscale;              // [B, H, D] (INT8 mode)
-  float* thr;                 // [B, N, H]
   int B, H, N, npad;
-  float s2, tau;
 };
 
 struct RouteParams {
   const __nv_bfloat16* kc;   // [B, Npad, H, D]
   const float* centroid;     // [B, N, H, D]
-  const float* thr;          // [B, N, H]
+  const float* kmean;        // [B, H, D] kc mean (BF16 mode; unused in INT8 mode)
+  const float* kvar;         // [B, H, D] kc variance (INT8: mean of centred kc^2)
+  float* thr;                // [B, N, H] written: the routing threshold of each q-block
   uint32_t* mask;            // [B, H, N, NW]
   int* count;                // [B, H, N]
   int* lists;                // [B, H, N, N] or null
   float* stat;               // [B, H, N, N] or null: (c . kc_j) * s2
   int B, H, N, npad, nw;
-  float s2;
+  float s2, tau;
+  int int8;                  // threshold formula of the INT8 path
   int sink_kv0, sink_kv1, sink_q0, sink_q1;
 };
 
@@ -69,5 +69,8 @@ void launch_quant_kv(const QuantParams& p, int hd, cudaStream_t st);
 void launch_morton(int64_t frames, int64_t height, int64_t width, int curve, int64_t roll,
                    int64_t* perm, int64_t* inverse, cudaStream_t st);
 void launch_gather(const GatherParams& p, cudaStream_t st);
+// bad[0] += quotients differing from __fdiv_rn, bad[1] += int8 codes differing
+void launch_quotient_selftest(const float* x, const float* s, int64_t n, unsigned long long* bad,
+                              cudaStream_t st);
 
 }  // namespace solb200

@@ -53,6 +53,7 @@ _SIGS = {
                                       c_void_p]),
     "solb200_copy_heads": (c_int32, [c_void_p, c_void_p, c_int64, c_int64, c_int64, c_int64, c_int64, c_int64,
                                      c_int32, c_void_p]),
+    "solb200_selftest_quotient": (c_int32, [c_void_p, c_void_p, c_int64, c_void_p, c_void_p]),
     "solb200_gather_rows": (c_int32, [POINTER(c_void_p), POINTER(c_void_p), c_int32, c_void_p, c_int64,
                                       c_int64, c_int64, c_int64, c_int64, c_int64, c_int64, c_void_p]),
 }

@@ -170,6 +170,14 @@ SOLB200_API int32_t solb200_gather_rows(const void* const* src, void* const* dst
                             int64_t src_stride_b, int64_t src_stride_row, int64_t dst_stride_b,
                             int64_t dst_stride_row, void* stream);
 
+/* Self-test of the arithmetic of the int8 quantisers (no counterpart in the
+ * reference): for n pairs (x[i], s[i]) of device float arrays (s > 0), adds to the
+ * device counters bad[0] the pairs whose division-free quotient differs from the
+ * IEEE quotient x/s, and to bad[1] those whose int8 code clamp(round half away from
+ * zero of x/s, +-127) differs. The caller zeroes bad (2 x uint64) first. */
+SOLB200_API int32_t solb200_selftest_quotient(const float* x, const float* s, int64_t n, uint64_t* bad,
+                                              void* stream);
+
 #ifdef __cplusplus
 }
 #endif
