@@ -33,7 +33,7 @@ struct Plan {
   int64_t B, T, H, D;
   int blk, N, npad, nw;
   bool int8;
-  int64_t off[17];
+  int64_t off[18];
   int64_t total;
 };
 
@@ -75,6 +75,7 @@ int32_t make_plan(int64_t B, int64_t T, int64_t H, int64_t D, int32_t blk, int32
     p.off[SOLB200_BUF_VI] = take(B * T * H * D);
   }
   p.off[SOLB200_BUF_ORDER] = take(B * H * p.N * 4);
+  if (p.int8 && D == 128 && blk == 128) p.off[SOLB200_BUF_VDQ] = take(B * T * H * D * 2);
   p.total = cur;
   return SOLB200_OK;
 }
@@ -228,6 +229,7 @@ int32_t run(const Plan& P, const Call& c) {
     qp.ki = at<int8_t>(c.ws, P, SOLB200_BUF_KI);
     qp.ks = at<float>(c.ws, P, SOLB200_BUF_KS);
     qp.vi = c.int8_pv ? at<int8_t>(c.ws, P, SOLB200_BUF_VI) : nullptr;
+    qp.vdq = c.int8_pv && P.off[SOLB200_BUF_VDQ] >= 0 ? at<__nv_bfloat16>(c.ws, P, SOLB200_BUF_VDQ) : nullptr;
     qp.B = (int)P.B; qp.T = (int)P.T; qp.H = (int)P.H; qp.tp = P.N * P.blk;
     launch_quant_kv(qp, hd, c.st);
   }
@@ -288,7 +290,12 @@ int32_t run(const Plan& P, const Call& c) {
   if ((rc = make_map(&m.ki, at<int8_t>(c.ws, P, SOLB200_BUF_KI), true, P.D, P.H, P.T, P.B, P.D, TD, P.T * TD,
                      P.blk, "ki")))
     return rc;
-  if (c.int8_pv) {
+  if (c.int8_pv && P.off[SOLB200_BUF_VDQ] >= 0) {
+    // the pipelined kernel's P.V operand: bf16 dequantised V, loaded like V
+    if ((rc = make_map(&m.vi, at<__nv_bfloat16>(c.ws, P, SOLB200_BUF_VDQ), false, P.D, P.H, P.T, P.B, P.D, TD,
+                       P.T * TD, kv_rows, "vdq")))
+      return rc;
+  } else if (c.int8_pv) {
     if ((rc = make_map(&m.vi, at<int8_t>(c.ws, P, SOLB200_BUF_VI), true, P.D, P.H, P.T, P.B, P.D, TD,
                        P.T * TD, P.blk, "vi")))
       return rc;
@@ -327,7 +334,7 @@ int32_t solb200_workspace_offset(int64_t batch, int64_t tokens, int64_t heads, i
   Plan p;
   const int32_t rc = make_plan(batch, tokens, heads, head_dim, block, int8, p);
   if (rc) return rc;
-  if (which < 0 || which > SOLB200_BUF_ORDER || p.off[which] < 0)
+  if (which < 0 || which > SOLB200_BUF_VDQ || p.off[which] < 0)
     return fail(SOLB200_ERR_INVALID, "buffer not part of this workspace");
   if (!offset) return fail(SOLB200_ERR_INVALID, "offset: null pointer");
   *offset = p.off[which];

@@ -7,25 +7,27 @@
 //     each pooled column by its block length (_int8_fwd.py:288-308).
 //   exact tiles (one routed 128-token block): S = qi . ki^T on kind::i8 (int32),
 //     scores = S * (qs * s2) * ks (_int8_fwd.py:311-332).
-//     INT8 P.V (int8_pv): pe = 2^(s - blockmax), pi = int8(min(pe*127 + 0.5, 127)) in
-//       shared memory, PV = pi . vi on kind::i8 into its own TMEM columns, folded into
-//       O by the softmax warps as O = O * alpha + PV * (beta / 127) * vscale[d] with
-//       beta = 2^(blockmax - m) (_int8_fwd.py:336-353).
+//     INT8 P.V (int8_pv, _int8_fwd.py:336-353): pe = 2^(s - blockmax), codes
+//       pi = int8(pe*127 rounded) as the reference; the reference's O += (pi . vi) *
+//       (beta / 127) * vscale[d] with beta = 2^(blockmax - m) is computed as
+//       P' = bf16(pi * beta / 127) (in TMEM, over the bf16 P columns) times
+//       vdq = bf16(vi * vscale) (the dequantised V, written by the preprocess), on
+//       kind::f16 accumulated into O by the tensor core: the int8 codes are the
+//       reference's, each operand carries one more bf16 rounding (2^-9 relative).
 //     BF16 P.V: P = 2^(s - m) in bf16 in TMEM, P . V (bf16) accumulated into O.
 //
 // One CTA per unit, one CTA per SM (all 512 TMEM columns):
-//   TMEM  [0,128) bf16 P (64 columns) or int32 P.V | [128,256) O | [256,384) S slot 0 |
+//   TMEM  [0,128) bf16 P (64 columns) | [128,256) O | [256,384) S slot 0 |
 //         [384,512) S slot 1
-//   smem  q bf16 32 KB | qi 16 KB | K ring 2 x 32 KB | V ring 2 x 32 KB | int8 P 16 KB |
-//         ks ring of 4 tiles, vscale, mask row, max / sum exchange
+//   smem  q bf16 32 KB | qi 16 KB | K ring 2 x 32 KB | V ring 2 x 32 KB |
+//         ks ring of 4 tiles, mask row, max / sum exchange
 // Warps 0-7 softmax (warps w and w+4 share the rows of TMEM lanes 32(w%4).. and split
 // each tile's 128 columns), warp 8 TMA producer, warp 9 TMEM allocator + MMA issuer.
 // The issuer keeps the tensor core idle while the softmax loads a tile's scores (a TMEM
 // load waits behind in-flight MMAs): per tile, the softmax loads S(j+1), then P.V(j)
-// and Q.K^T(j+2) run while it works on tile j+1. The fold of an int8 P.V(j) into O is
-// done by the softmax warps when they next need the P / P.V columns (tile j+1, or the
-// epilogue). Every wait is bounded; every softmax thread runs every tile and every
-// named barrier, also after a failed wait (the work is skipped, the barriers are not).
+// and Q.K^T(j+2) run while it works on tile j+1. Every wait is bounded; every softmax
+// thread runs every tile and every named barrier, also after a failed wait (the work is
+// skipped, the barriers are not).
 #include "common.cuh"
 #include "fwd_common.cuh"
 
@@ -79,36 +81,34 @@ __device__ __forceinline__ float exp_bf16_64(uint32_t (&r)[64], float sc, float 
   return sum;
 }
 
-// int32 -> float without the conversion unit (which the exponentials share): for
-// |x| < 2^22 the bits 0x4B400000 + x are the float 1.5*2^23 + x, exact; removing
-// 1.5*2^23 leaves float(x) exactly. Scores qi . ki are below 128 * 127^2 < 2^22.
-__device__ __forceinline__ float i2f_exact(uint32_t x) {
-  return __uint_as_float(x + 0x4B400000u) - 12582912.f;
+// int32 -> float without the conversion unit (which the exponentials share), two at a
+// time: for |x| < 2^22 the bits 0x4B400000 + x are the float 1.5*2^23 + x, exact;
+// removing 1.5*2^23 (a packed add) leaves float(x) exactly. Scores qi . ki and int8
+// P.V sums are below 128 * 127^2 < 2^22.
+__device__ __forceinline__ float2 i2f_exact2(uint32_t x, uint32_t y) {
+  return add2(make_float2(__uint_as_float(x + 0x4B400000u), __uint_as_float(y + 0x4B400000u)),
+              make_float2(-12582912.f, -12582912.f));
 }
 
-// pe = 2^(r - bm) in [0, 1] for the 64 columns (log2-unit scores in r); the int8 codes
-// min(pe*127 + 0.5, 127) truncated (_int8_fwd.py:350) packed four per word into q[16];
-// returns the sum of pe. The truncation of y in [0.5, 127] is the low byte of
-// y + 2^23 rounded toward zero (an FMA-pipe add instead of a conversion).
-__device__ __forceinline__ float exp_int8_64(const uint32_t (&r)[64], float bm, uint32_t (&q)[16]) {
+// Exact tile with int8 P.V semantics: pe = 2^(r * sc - bm) in [0, 1] for the 64 columns
+// (r: scores before the per-row factor sc; bm: the tile's row max in log2 units); the
+// int8 code of pe (_int8_fwd.py:350: min(pe*127 + 0.5, 127) truncated) is the low part
+// of RN(pe*127 + 2^23) = 2^23 + pe*127 rounded to the nearest integer (the reference's
+// rounding except at exact ties, half-even here; the clamp never binds as pe <= 1);
+// P' = code * pscale (= beta / 127) as bf16 pairs in r[0..31]; returns the sum of pe.
+// Packed f32x2 arithmetic throughout.
+__device__ __forceinline__ float exp_int8p_bf16_64(uint32_t (&r)[64], float sc, float bm, float pscale) {
   float2 acc = make_float2(0.f, 0.f);
+  const float2 scv = make_float2(sc, sc), nbm = make_float2(-bm, -bm);
+  const float2 k127 = make_float2(127.f, 127.f), mg = make_float2(8388608.f, 8388608.f);
+  const float2 nmg = make_float2(-8388608.f, -8388608.f), ps = make_float2(pscale, pscale);
 #pragma unroll
-  for (int w = 0; w < 16; ++w) {
-    uint32_t b[4];
-#pragma unroll
-    for (int e = 0; e < 4; e += 2) {
-      const float2 pe = make_float2(fast_exp2(__uint_as_float(r[w * 4 + e]) - bm),
-                                    fast_exp2(__uint_as_float(r[w * 4 + e + 1]) - bm));
-      acc = add2(acc, pe);
-      b[e] = __float_as_uint(__fadd_rz(fminf(__fadd_rn(__fmul_rn(pe.x, 127.f), 0.5f), 127.f), 8388608.f));
-      b[e + 1] = __float_as_uint(__fadd_rz(fminf(__fadd_rn(__fmul_rn(pe.y, 127.f), 0.5f), 127.f), 8388608.f));
-    }
-    // low bytes of b[0], b[1] -> bytes 0, 1 of lo (likewise hi); then lo.0 lo.1 hi.0 hi.1
-    uint32_t lo, hi, word;
-    asm("prmt.b32 %0, %1, %2, 0x0040;" : "=r"(lo) : "r"(b[0]), "r"(b[1]));
-    asm("prmt.b32 %0, %1, %2, 0x0040;" : "=r"(hi) : "r"(b[2]), "r"(b[3]));
-    asm("prmt.b32 %0, %1, %2, 0x5410;" : "=r"(word) : "r"(lo), "r"(hi));
-    q[w] = word;
+  for (int i = 0; i < 64; i += 2) {
+    const float2 x = fma2(make_float2(__uint_as_float(r[i]), __uint_as_float(r[i + 1])), scv, nbm);
+    const float2 pe = make_float2(fast_exp2(x.x), fast_exp2(x.y));
+    acc = add2(acc, pe);
+    const float2 v = mul2(add2(fma2(pe, k127, mg), nmg), ps);   // code * beta / 127
+    r[i >> 1] = pack_bf16x2(v.x, v.y);
   }
   return acc.x + acc.y;
 }
@@ -121,6 +121,7 @@ sol_fwd_int8p_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_cons
                      const __grid_constant__ CUtensorMap tm_qi, const __grid_constant__ CUtensorMap tm_ki,
                      const __grid_constant__ CUtensorMap tm_vi, const __grid_constant__ CUtensorMap tm_v,
                      const FwdParams p) {
+  pdl_begin();
   constexpr int HD = 128, BLK = 128;
   constexpr uint32_t BOX = 128 * 128;           // 128 rows x 128 bytes
   constexpr uint32_t TILE = 2 * BOX;            // 128 rows x 128 bf16
@@ -128,25 +129,22 @@ sol_fwd_int8p_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_cons
   constexpr uint32_t IDESC_QK_BF16 = make_idesc(kFmtF32, kFmtBF16, kFmtBF16, 0, 0, 128, 128);
   constexpr uint32_t IDESC_PV_BF16 = make_idesc(kFmtF32, kFmtBF16, kFmtBF16, 0, 1, 128, HD);
   constexpr uint32_t IDESC_QK_I8 = make_idesc(kFmtS32, kFmtS8, kFmtS8, 0, 0, 128, 128);
-  constexpr uint32_t IDESC_PV_I8 = make_idesc(kFmtS32, kFmtS8, kFmtS8, 0, 1, 128, HD);
 
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sQ = smem;                    // bf16 q (approximate tiles); later the O staging
   uint8_t* sQI = sQ + TILE;              // int8 qi, 128 rows x 128 bytes
   uint8_t* sK = sQI + BOX;               // KST stages: kc (bf16, 32 KB) or ki (int8, 16 KB)
-  uint8_t* sV = sK + KST * TILE;         // VST stages: vc / v (bf16) or vi (int8)
-  uint8_t* sP = sV + VST * TILE;         // int8 P, 128 rows x 128 bytes
-  float* sKS = reinterpret_cast<float*>(sP + BOX);   // [4][128] key scales, by tile j % 4
-  float* sVSC = sKS + 4 * 128;                       // [HD] value scales
-  uint64_t* bars = reinterpret_cast<uint64_t*>(sVSC + HD);
-  uint64_t* bar_q = bars + 0;            // q, qi, vscale staged
+  uint8_t* sV = sK + KST * TILE;         // VST stages: vc, v or vdq (bf16)
+  float* sKS = reinterpret_cast<float*>(sV + VST * TILE);   // [4][128] key scales, by tile j % 4
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sKS + 4 * 128);
+  uint64_t* bar_q = bars + 0;            // q, qi staged
   uint64_t* bar_kfull = bars + 1;        // [KST]
   uint64_t* bar_kfree = bars + 3;        // [KST] Q.K^T of the stage's tile complete
   uint64_t* bar_vfull = bars + 5;        // [VST]
   uint64_t* bar_vfree = bars + 7;        // [VST] P.V of the stage's tile complete
   uint64_t* bar_sfree = bars + 9;        // [2] scores of a slot loaded by the softmax (256)
-  uint64_t* bar_pfull = bars + 11;       // P written, previous int8 P.V folded (256)
+  uint64_t* bar_pfull = bars + 11;       // P written (256)
   uint64_t* bar_drain = bars + 12;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 13);
   uint32_t* sMask = reinterpret_cast<uint32_t*>(bars + 16);    // kMaskCapI8 words
@@ -191,7 +189,7 @@ sol_fwd_int8p_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_cons
 
   if (warp == 8) {
     // ------------------------------------------------------------ TMA producer
-    // q, qi, vscale; K0 K1, V0 V1; then per tile j: K(j+2) once Q.K^T(j) is done with
+    // q, qi; K0 K1, V0 V1; then per tile j: K(j+2) once Q.K^T(j) is done with
     // its stage (its key scales go to ring slot (j+2) % 4, which the softmax finished
     // with at tile j-2), V(j+2) once P.V(j) is done.
     if (lane == 0) {
@@ -201,10 +199,9 @@ sol_fwd_int8p_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_cons
       tma_prefetch_desc(&tm_qi);
       tma_prefetch_desc(&tm_ki);
       tma_prefetch_desc(pv8 ? &tm_vi : &tm_v);
-      mbar_arrive_expect_tx(bar_q, TILE + BOX + (pv8 ? HD * 4 : 0));
+      mbar_arrive_expect_tx(bar_q, TILE + BOX);
       for (int i = 0; i < 2; ++i) tma_load_4d(sQ + i * BOX, &tm_q, bar_q, i * 64, u.h, u.qb * BLK, u.b);
       tma_load_4d(sQI, &tm_qi, bar_q, 0, u.h, u.qb * BLK, u.b);
-      if (pv8) bulk_load(sVSC, p.vscale + (int64_t)bh * HD, HD * 4, bar_q);
       auto load_k = [&](int stage, int kind, int idx, int jt) {
         uint64_t* bar = bar_kfull + stage;
         uint8_t* dst = sK + stage * TILE;
@@ -223,12 +220,11 @@ sol_fwd_int8p_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_cons
         if (kind == kTileApprox) {
           mbar_arrive_expect_tx(bar, TILE);
           for (int i = 0; i < 2; ++i) tma_load_4d(dst + i * BOX, &tm_vc, bar, i * 64, u.h, idx * 128, u.b);
-        } else if (pv8) {
-          mbar_arrive_expect_tx(bar, BOX);
-          tma_load_4d(dst, &tm_vi, bar, 0, u.h, idx * BLK, u.b);
         } else {
+          // exact tile: the bf16 dequantised V (int8_pv; tm_vi maps it) or V
+          const CUtensorMap* tmv = pv8 ? &tm_vi : &tm_v;
           mbar_arrive_expect_tx(bar, TILE);
-          for (int i = 0; i < 2; ++i) tma_load_4d(dst + i * BOX, &tm_v, bar, i * 64, u.h, idx * BLK, u.b);
+          for (int i = 0; i < 2; ++i) tma_load_4d(dst + i * BOX, tmv, bar, i * 64, u.h, idx * BLK, u.b);
         }
       };
       TileIter itk(p, u), itv(p, u);
@@ -270,8 +266,6 @@ sol_fwd_int8p_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_cons
       const uint64_t qid = make_sw128_desc(smem_u32(sQI), 16, 1024);
       const uint64_t kd0 = make_sw128_desc(smem_u32(sK), 16, 1024);
       const uint64_t vd0 = make_sw128_desc(smem_u32(sV), BOX, 1024);   // bf16 V, MN-major
-      const uint64_t vid0 = make_sw128_desc(smem_u32(sV), 0, 1024);    // int8 V, MN-major
-      const uint64_t pd = make_sw128_desc(smem_u32(sP), 16, 1024);     // int8 P, K-major
       auto issue_qk = [&](int j, int kind) {
         const int st = j % KST;
         const uint32_t d = tS + (j & 1) * 128;
@@ -312,11 +306,7 @@ sol_fwd_int8p_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_cons
         if (!(ok = mbar_wait(bar_vfull + j % VST, (j / VST) & 1, p.err, kErrWaitMma))) break;
         tc_fence_after();
         const uint32_t vo = (j % VST) * (TILE >> 4);
-        if (kind == kTileExact && pv8) {
-#pragma unroll
-          for (int kk = 0; kk < BLK / 32; ++kk)
-            mma_i8_ss(tA, pd + (uint64_t)(kk * 2), vid0 + (uint64_t)(vo + kk * (4096 >> 4)), IDESC_PV_I8, kk > 0);
-        } else {
+        {
           const uint32_t acc0 = j > 0 ? 1u : 0u;
 #pragma unroll
           for (int kk = 0; kk < 8; ++kk)
@@ -336,44 +326,16 @@ sol_fwd_int8p_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_cons
       mbar_wait(bar_drain, 0, p.err, kErrWaitDrain);
     }
   } else {
-    // -------------------------------- softmax, folds, epilogue (rows x column halves)
+    // -------------------------------- softmax and epilogue (rows x column halves)
     const int row = threadIdx.x & 127;                 // TMEM lane / query row
     const int h = threadIdx.x >> 7;                    // column half of tiles and of O
     const uint32_t lane_base = (uint32_t)((warp & 3) * 32) << 16;
     const int qrow = u.qb * BLK + row;
     const float qs_log2 = (qrow < p.T ? __ldg(p.qs + (int64_t)bh * tp + qrow) : 0.f) * p.s2;
-    bool ok = mbar_wait_warp(bar_q, 0, p.err, kErrWaitSoftmax);   // vscale is staged with q
+    bool ok = mbar_wait_warp(bar_q, 0, p.err, kErrWaitSoftmax);
     float m_ref = -INFINITY, l_sum = 0.f;
     bool o_live = false;      // O holds a contribution
-    bool fold_pending = false;
-    float f_alpha = 1.f, f_scale = 0.f;   // the pending int8 P.V fold: O*alpha + PV*scale*vscale
     int j = 0, kind, idx;
-    // fold an int8 P.V (complete) into this thread's half of O
-    auto fold = [&]() {
-      if (!ok) return;
-#pragma unroll 1
-      for (int c = 0; c < 2; ++c) {
-        uint32_t pv[32], o[32];
-        tmem_ld32(tA + lane_base + h * 64 + c * 32, pv);
-        if (o_live) tmem_ld32(tO + lane_base + h * 64 + c * 32, o);
-        tmem_wait_ld();
-        const float4* vs4 = reinterpret_cast<const float4*>(sVSC + h * 64 + c * 32);
-#pragma unroll
-        for (int i = 0; i < 32; i += 4) {
-          const float4 v4 = vs4[i >> 2];
-          const float vv[4] = {v4.x, v4.y, v4.z, v4.w};
-#pragma unroll
-          for (int e = 0; e < 4; ++e) {
-            // |P.V| <= 128 * 127 * 127 < 2^22: exact through the magic-number conversion
-            const float add = i2f_exact(pv[i + e]) * (f_scale * vv[e]);
-            o[i + e] = __float_as_uint(o_live ? fmaf(__uint_as_float(o[i + e]), f_alpha, add) : add);
-          }
-        }
-        tmem_st32(tO + lane_base + h * 64 + c * 32, o);
-      }
-      tmem_wait_st();
-      o_live = true;
-    };
     TileIter it(p, u);
     for (; it.next(kind, idx); ++j) {
       const bool exact = kind == kTileExact;
@@ -388,15 +350,18 @@ sol_fwd_int8p_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_cons
       tc_fence_before();
       mbar_arrive(bar_sfree + (j & 1));
       if (ok && exact) {
-        // int32 scores -> log2 units: * (qs * s2) * ks (_int8_fwd.py:329-330)
+        // int32 scores * ks (_int8_fwd.py:329-330); the per-row factor qs * s2 (positive)
+        // is applied to the row max and inside the exponent
         const float4* ks4 = reinterpret_cast<const float4*>(sKS + (j & 3) * 128 + h * 64);
 #pragma unroll
         for (int i = 0; i < 64; i += 4) {
           const float4 k4 = ks4[i >> 2];
-          r[i] = __float_as_uint(i2f_exact(r[i]) * (qs_log2 * k4.x));
-          r[i + 1] = __float_as_uint(i2f_exact(r[i + 1]) * (qs_log2 * k4.y));
-          r[i + 2] = __float_as_uint(i2f_exact(r[i + 2]) * (qs_log2 * k4.z));
-          r[i + 3] = __float_as_uint(i2f_exact(r[i + 3]) * (qs_log2 * k4.w));
+          const float2 s01 = mul2(i2f_exact2(r[i], r[i + 1]), make_float2(k4.x, k4.y));
+          const float2 s23 = mul2(i2f_exact2(r[i + 2], r[i + 3]), make_float2(k4.z, k4.w));
+          r[i] = __float_as_uint(s01.x);
+          r[i + 1] = __float_as_uint(s01.y);
+          r[i + 2] = __float_as_uint(s23.x);
+          r[i + 3] = __float_as_uint(s23.y);
         }
       }
       // P.V(j-1) complete: the P / P.V columns and the int8 P buffer are free again
@@ -420,7 +385,7 @@ sol_fwd_int8p_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_cons
         masked = idx * BLK + BLK > p.T;
       }
       const uint32_t cm[2] = {h ? colmask[2] : colmask[0], h ? colmask[3] : colmask[1]};
-      const float sc = exact ? 1.f : p.s2;   // scores -> log2 units
+      const float sc = exact ? qs_log2 : p.s2;   // scores -> log2 units (both positive)
       float pm = -INFINITY;
       if (ok) pm = (masked ? max64<true>(r, cm) : max64<false>(r, cm)) * sc;
       float* xm = sMax + (j & 1) * 256;
@@ -437,59 +402,40 @@ sol_fwd_int8p_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_cons
         m_ref = m_new;
         need = true;
       }
+      // P in TMEM as bf16, P.V accumulated into O by the tensor core; O is rescaled first
+      // when a row's reference max moved (warp-uniform, after P.V(j-1) is complete)
+      if (__any_sync(0xffffffffu, need) && o_live) {
+        wait_pv();
+        if (ok) rescale_rows<64>(tO + lane_base + h * 64, alpha);
+      }
+      float psum = 0.f;
       if (exact && pv8) {
-        // ------------------------------ int8 P (relative to the tile's max) -> smem
+        // int8 P relative to the tile's max, scaled by beta / 127 (see exp_int8p_bf16_64)
         const float bm = mx;
         const float beta = mx == -INFINITY ? 0.f : fast_exp2(bm - m_ref);
-        uint32_t q[16];
-        float psum = 0.f;
-        if (ok) psum = exp_int8_64(r, bm == -INFINITY ? 0.f : bm, q);
+        if (ok) psum = exp_int8p_bf16_64(r, sc, bm == -INFINITY ? 0.f : bm, beta * (1.0f / 127.0f));
         l_sum = l_sum * alpha + beta * psum;
-        wait_pv();                       // int8 P buffer and P.V columns free
-        if (fold_pending) fold();        // P.V(j-1) into O before P.V(j) overwrites it
-        fold_pending = false;
-        if (ok) {
-          // this half's 64 bytes of the row: 16-byte chunks 4h..4h+3, 128-byte swizzle
-#pragma unroll
-          for (int c = 0; c < 4; ++c) {
-            const int chunk = h * 4 + c;
-            *reinterpret_cast<uint4*>(sP + row * 128 + ((chunk ^ (row & 7)) << 4)) =
-                make_uint4(q[c * 4], q[c * 4 + 1], q[c * 4 + 2], q[c * 4 + 3]);
-          }
-        }
-        fence_proxy_async_smem();        // generic stores -> tensor core (async proxy)
-        f_alpha = alpha;
-        f_scale = beta * (1.0f / 127.0f);
-        fold_pending = true;
       } else {
-        // ------------------------------ bf16 P in TMEM, P.V accumulated by the MMA
-        if (__any_sync(0xffffffffu, need) && o_live) {
-          wait_pv();
-          l_sum *= alpha;
-          if (ok) rescale_rows<64>(tO + lane_base + h * 64, alpha);
-        }
         const float m_use = m_ref == -INFINITY ? 0.f : m_ref;
-        float psum = 0.f;
         if (ok)
           psum = exact ? exp_bf16_64<false>(r, sc, m_use, -1, 0.f, 1.f)
                        : exp_bf16_64<true>(r, sc, m_use, tail_col, (float)(p.T - (p.N - 1) * BLK), (float)BLK);
-        l_sum += psum;
-        wait_pv();                       // P columns free
-        if (ok) {
-          tmem_st32(tA + lane_base + h * 32, *reinterpret_cast<const uint32_t(*)[32]>(&r[0]));
-          tmem_wait_st();
-        }
-        o_live = true;
+        l_sum = l_sum * alpha + psum;
       }
+      wait_pv();                       // P columns free
+      if (ok) {
+        tmem_st32(tA + lane_base + h * 32, *reinterpret_cast<const uint32_t(*)[32]>(&r[0]));
+        tmem_wait_st();
+      }
+      o_live = true;
       tc_fence_before();
       mbar_arrive(bar_pfull);
     }
-    // epilogue: the last P.V (and its fold), l = both halves' sums, O / l -> bf16 ->
-    // swizzled staging (the q buffer) -> TMA store when every softmax thread succeeded
+    // epilogue: the last P.V, l = both halves' sums, O / l -> bf16 -> swizzled staging
+    // (the q buffer) -> TMA store when every softmax thread succeeded
     if (j > 0 && ok) {
       ok = mbar_wait_warp(bar_vfree + (j - 1) % VST, ((j - 1) / VST) & 1, p.err, kErrWaitEpilogue);
       tc_fence_after();
-      if (fold_pending) fold();
     }
     sSum[h * 128 + row] = l_sum;
     if (!ok) *sBad = 1;
@@ -533,11 +479,11 @@ sol_fwd_int8p_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_cons
   }
 }
 
-// q 32 KB + qi 16 KB + K ring 64 KB + V ring 64 KB + P 16 KB + scales + barriers +
-// mask row + exchange, plus 1 KB to align the tiles to 1024 bytes
+// q 32 KB + qi 16 KB + K ring 64 KB + V ring 64 KB + key scales + barriers + mask row +
+// exchange, plus 1 KB to align the tiles to 1024 bytes
 size_t fwd_int8p_smem_bytes() {
-  return (size_t)(2 * 16384 + 16384 + 2 * 32768 + 2 * 32768 + 16384) + 4 * 128 * 4 + 128 * 4 + 128 +
-         4 * kMaskCapI8 + 4 * (512 + 256) + 16 + 1024;
+  return (size_t)(2 * 16384 + 16384 + 2 * 32768 + 2 * 32768) + 4 * 128 * 4 + 128 + 4 * kMaskCapI8 +
+         4 * (512 + 256) + 16 + 1024;
 }
 
 cudaError_t launch_fwd_int8p(const FwdMaps& m, const FwdParams& p, cudaStream_t st) {
@@ -545,8 +491,8 @@ cudaError_t launch_fwd_int8p(const FwdMaps& m, const FwdParams& p, cudaStream_t 
   cudaError_t e = cudaFuncSetAttribute(sol_fwd_int8p_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return e;
   const unsigned grid = (unsigned)((int64_t)p.B * p.H * p.N);
-  sol_fwd_int8p_kernel<<<grid, 320, smem, st>>>(m.q, m.kc, m.vc, m.o, m.qi, m.ki, m.vi, m.v, p);
-  return cudaGetLastError();
+  return launch_pdl(sol_fwd_int8p_kernel, dim3(grid), dim3(320), smem, st, m.q, m.kc, m.vc, m.o, m.qi,
+                    m.ki, m.vi, m.v, p);
 }
 
 }  // namespace solb200

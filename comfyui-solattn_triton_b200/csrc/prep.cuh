@@ -48,6 +48,7 @@ struct QuantParams {
   const float* vscale;   // [B, H, D] or null
   int8_t* ki; float* ks; // [B, T, H, D], [B, H, tp]
   int8_t* vi;            // [B, T, H, D] or null
+  __nv_bfloat16* vdq;    // [B, T, H, D] bf16(vi * vscale), or null
   int B, T, H, tp;       // tp = N * blk (row stride of ks)
 };
 

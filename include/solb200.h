@@ -75,9 +75,12 @@ enum solb200_buffer {
   SOLB200_BUF_KI = 13,        /* int8 [B, T, H, D] (INT8) */
   SOLB200_BUF_KS = 14,        /* fp32 [B, H, N*block] (INT8; entries >= T unused) */
   SOLB200_BUF_VI = 15,        /* int8 [B, T, H, D] (INT8) */
-  SOLB200_BUF_ORDER = 16      /* int32 [B*H*N] the forward's schedule: unit ids (b*H + h)*N + n,
+  SOLB200_BUF_ORDER = 16,     /* int32 [B*H*N] the forward's schedule: unit ids (b*H + h)*N + n,
                                  head by head, each head's query blocks by descending
                                  exact-block count (the cheapest units run last) */
+  SOLB200_BUF_VDQ = 17        /* bf16 [B, T, H, D] dequantised V, vi * vscale rounded to bf16:
+                                 the P.V operand of the INT8 forward with int8_pv (head_dim
+                                 128, block 128 only; absent otherwise) */
 };
 
 /* Thread-local text of the last failure (empty string if none). */
