@@ -309,7 +309,8 @@ def run_ours(args, rank, world, local_rank):
                  "h2d_bytes_per_step": h2d * world, "d2h_bytes_per_step": d2h * world,
                  "api": "solb200.sol_attn_host (pinned host in and out, head chunks streamed)"}
                 if ms_e2e else None),
-        "gpu_launches": 4 * args.steps + (1 if int8 else 0) * args.steps,
+        # per step: pool, moments, route, order, forward (+ quant_kv on the INT8 path)
+        "gpu_launches": (5 + (1 if int8 else 0)) * args.steps,
         "clocks": clocks,
     }
     return result

@@ -101,13 +101,14 @@ __device__ __forceinline__ float exp_int8p_bf16_64(uint32_t (&r)[64], float sc, 
   float2 acc = make_float2(0.f, 0.f);
   const float2 scv = make_float2(sc, sc), nbm = make_float2(-bm, -bm);
   const float2 k127 = make_float2(127.f, 127.f), mg = make_float2(8388608.f, 8388608.f);
-  const float2 nmg = make_float2(-8388608.f, -8388608.f), ps = make_float2(pscale, pscale);
+  // (c - 2^23) * ps as one FMA: c * ps - 2^23 * ps, the product by 2^23 exact
+  const float2 ps = make_float2(pscale, pscale), nps = make_float2(-8388608.f * pscale, -8388608.f * pscale);
 #pragma unroll
   for (int i = 0; i < 64; i += 2) {
     const float2 x = fma2(make_float2(__uint_as_float(r[i]), __uint_as_float(r[i + 1])), scv, nbm);
     const float2 pe = make_float2(fast_exp2(x.x), fast_exp2(x.y));
     acc = add2(acc, pe);
-    const float2 v = mul2(add2(fma2(pe, k127, mg), nmg), ps);   // code * beta / 127
+    const float2 v = fma2(fma2(pe, k127, mg), ps, nps);   // code * beta / 127
     r[i >> 1] = pack_bf16x2(v.x, v.y);
   }
   return acc.x + acc.y;
