@@ -33,7 +33,7 @@ struct Plan {
   int64_t B, T, H, D;
   int blk, N, npad, nw;
   bool int8;
-  int64_t off[18];
+  int64_t off[20];
   int64_t total;
 };
 
@@ -75,7 +75,11 @@ int32_t make_plan(int64_t B, int64_t T, int64_t H, int64_t D, int32_t blk, int32
     p.off[SOLB200_BUF_VI] = take(B * T * H * D);
   }
   p.off[SOLB200_BUF_ORDER] = take(B * H * p.N * 4);
-  if (p.int8 && D == 128 && blk == 128) p.off[SOLB200_BUF_VDQ] = take(B * T * H * D * 2);
+  if (p.int8 && D == 128 && blk == 128) {   // operands of the pipelined INT8 forward
+    p.off[SOLB200_BUF_VDQ] = take(B * T * H * D * 2);
+    p.off[SOLB200_BUF_QIB] = take(B * T * H * D * 2);
+    p.off[SOLB200_BUF_KIB] = take(B * T * H * D * 2);
+  }
   p.total = cur;
   return SOLB200_OK;
 }
@@ -205,6 +209,7 @@ int32_t run(const Plan& P, const Call& c) {
   pp.centroid = at<float>(c.ws, P, SOLB200_BUF_CENTROID);
   pp.vamax = (c.int8 && c.int8_pv) ? at<float>(c.ws, P, SOLB200_BUF_VAMAX) : nullptr;
   pp.qi = c.int8 ? at<int8_t>(c.ws, P, SOLB200_BUF_QI) : nullptr;
+  pp.qib = c.int8 && P.off[SOLB200_BUF_QIB] >= 0 ? at<__nv_bfloat16>(c.ws, P, SOLB200_BUF_QIB) : nullptr;
   pp.qs = c.int8 ? at<float>(c.ws, P, SOLB200_BUF_QS) : nullptr;
   pp.B = (int)P.B; pp.T = (int)P.T; pp.H = (int)P.H; pp.N = P.N; pp.npad = P.npad; pp.blk = P.blk;
   pp.tp = P.N * P.blk;
@@ -227,6 +232,7 @@ int32_t run(const Plan& P, const Call& c) {
     qp.kmean = mp.kmean;
     qp.vscale = c.int8_pv ? mp.vscale : nullptr;
     qp.ki = at<int8_t>(c.ws, P, SOLB200_BUF_KI);
+    qp.kib = P.off[SOLB200_BUF_KIB] >= 0 ? at<__nv_bfloat16>(c.ws, P, SOLB200_BUF_KIB) : nullptr;
     qp.ks = at<float>(c.ws, P, SOLB200_BUF_KS);
     qp.vi = c.int8_pv ? at<int8_t>(c.ws, P, SOLB200_BUF_VI) : nullptr;
     qp.vdq = c.int8_pv && P.off[SOLB200_BUF_VDQ] >= 0 ? at<__nv_bfloat16>(c.ws, P, SOLB200_BUF_VDQ) : nullptr;
@@ -286,10 +292,18 @@ int32_t run(const Plan& P, const Call& c) {
     return SOLB200_OK;
   }
   const int64_t TD = P.H * P.D;
-  if ((rc = make_map(&m.qi, pp.qi, true, P.D, P.H, P.T, P.B, P.D, TD, P.T * TD, 128, "qi"))) return rc;
-  if ((rc = make_map(&m.ki, at<int8_t>(c.ws, P, SOLB200_BUF_KI), true, P.D, P.H, P.T, P.B, P.D, TD, P.T * TD,
-                     P.blk, "ki")))
-    return rc;
+  if (P.off[SOLB200_BUF_QIB] >= 0) {
+    // the pipelined kernel's Q.K^T operands: the int8 codes as bf16, loaded like q and k
+    if ((rc = make_map(&m.qi, pp.qib, false, P.D, P.H, P.T, P.B, P.D, TD, P.T * TD, 128, "qib"))) return rc;
+    if ((rc = make_map(&m.ki, at<__nv_bfloat16>(c.ws, P, SOLB200_BUF_KIB), false, P.D, P.H, P.T, P.B, P.D, TD,
+                       P.T * TD, kv_rows, "kib")))
+      return rc;
+  } else {
+    if ((rc = make_map(&m.qi, pp.qi, true, P.D, P.H, P.T, P.B, P.D, TD, P.T * TD, 128, "qi"))) return rc;
+    if ((rc = make_map(&m.ki, at<int8_t>(c.ws, P, SOLB200_BUF_KI), true, P.D, P.H, P.T, P.B, P.D, TD, P.T * TD,
+                       P.blk, "ki")))
+      return rc;
+  }
   if (c.int8_pv && P.off[SOLB200_BUF_VDQ] >= 0) {
     // the pipelined kernel's P.V operand: bf16 dequantised V, loaded like V
     if ((rc = make_map(&m.vi, at<__nv_bfloat16>(c.ws, P, SOLB200_BUF_VDQ), false, P.D, P.H, P.T, P.B, P.D, TD,
@@ -334,7 +348,7 @@ int32_t solb200_workspace_offset(int64_t batch, int64_t tokens, int64_t heads, i
   Plan p;
   const int32_t rc = make_plan(batch, tokens, heads, head_dim, block, int8, p);
   if (rc) return rc;
-  if (which < 0 || which > SOLB200_BUF_VDQ || p.off[which] < 0)
+  if (which < 0 || which > SOLB200_BUF_KIB || p.off[which] < 0)
     return fail(SOLB200_ERR_INVALID, "buffer not part of this workspace");
   if (!offset) return fail(SOLB200_ERR_INVALID, "offset: null pointer");
   *offset = p.off[which];

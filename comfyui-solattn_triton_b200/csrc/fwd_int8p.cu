@@ -5,8 +5,11 @@
 //   approximate tiles (128 pooled keys): bf16 q . kc^T (kind::f16, q and kc in shared
 //     memory), bf16 P . vc accumulated into O by the tensor core; the row sum weighs
 //     each pooled column by its block length (_int8_fwd.py:288-308).
-//   exact tiles (one routed 128-token block): S = qi . ki^T on kind::i8 (int32),
-//     scores = S * (qs * s2) * ks (_int8_fwd.py:311-332).
+//   exact tiles (one routed 128-token block): S = qi . ki^T (_int8_fwd.py:311-332) on
+//     kind::f16 over the int8 codes held as bf16 (qib, kib, written by the preprocess):
+//     every product (<= 127^2) and partial sum (< 2^21) is an integer that fp32 holds
+//     exactly, so S arrives in TMEM as the exact integer dot in fp32;
+//     scores = S * (qs * s2) * ks.
 //     INT8 P.V (int8_pv, _int8_fwd.py:336-353): pe = 2^(s - blockmax), codes
 //       pi = int8(pe*127 rounded) as the reference; the reference's O += (pi . vi) *
 //       (beta / 127) * vscale[d] with beta = 2^(blockmax - m) is computed as
@@ -19,7 +22,7 @@
 // One CTA per unit, one CTA per SM (all 512 TMEM columns):
 //   TMEM  [0,128) bf16 P (64 columns) | [128,256) O | [256,384) S slot 0 |
 //         [384,512) S slot 1
-//   smem  q bf16 32 KB | qi 16 KB | K ring 2 x 32 KB | V ring 2 x 32 KB |
+//   smem  q bf16 32 KB | qi codes bf16 32 KB | K ring 2 x 32 KB | V ring 2 x 32 KB |
 //         ks ring of 4 tiles, mask row, max / sum exchange
 // Warps 0-7 softmax (warps w and w+4 share the rows of TMEM lanes 32(w%4).. and split
 // each tile's 128 columns), warp 8 TMA producer, warp 9 TMEM allocator + MMA issuer.
@@ -81,15 +84,6 @@ __device__ __forceinline__ float exp_bf16_64(uint32_t (&r)[64], float sc, float 
   return sum;
 }
 
-// int32 -> float without the conversion unit (which the exponentials share), two at a
-// time: for |x| < 2^22 the bits 0x4B400000 + x are the float 1.5*2^23 + x, exact;
-// removing 1.5*2^23 (a packed add) leaves float(x) exactly. Scores qi . ki and int8
-// P.V sums are below 128 * 127^2 < 2^22.
-__device__ __forceinline__ float2 i2f_exact2(uint32_t x, uint32_t y) {
-  return add2(make_float2(__uint_as_float(x + 0x4B400000u), __uint_as_float(y + 0x4B400000u)),
-              make_float2(-12582912.f, -12582912.f));
-}
-
 // Exact tile with int8 P.V semantics: pe = 2^(r * sc - bm) in [0, 1] for the 64 columns
 // (r: scores before the per-row factor sc; bm: the tile's row max in log2 units); the
 // int8 code of pe (_int8_fwd.py:350: min(pe*127 + 0.5, 127) truncated) is the low part
@@ -129,13 +123,12 @@ sol_fwd_int8p_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_cons
   constexpr int KST = 2, VST = 2;
   constexpr uint32_t IDESC_QK_BF16 = make_idesc(kFmtF32, kFmtBF16, kFmtBF16, 0, 0, 128, 128);
   constexpr uint32_t IDESC_PV_BF16 = make_idesc(kFmtF32, kFmtBF16, kFmtBF16, 0, 1, 128, HD);
-  constexpr uint32_t IDESC_QK_I8 = make_idesc(kFmtS32, kFmtS8, kFmtS8, 0, 0, 128, 128);
 
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sQ = smem;                    // bf16 q (approximate tiles); later the O staging
-  uint8_t* sQI = sQ + TILE;              // int8 qi, 128 rows x 128 bytes
-  uint8_t* sK = sQI + BOX;               // KST stages: kc (bf16, 32 KB) or ki (int8, 16 KB)
+  uint8_t* sQI = sQ + TILE;              // qi codes as bf16, 128 rows x 128 columns
+  uint8_t* sK = sQI + TILE;              // KST stages: kc or the ki codes (bf16, 32 KB)
   uint8_t* sV = sK + KST * TILE;         // VST stages: vc, v or vdq (bf16)
   float* sKS = reinterpret_cast<float*>(sV + VST * TILE);   // [4][128] key scales, by tile j % 4
   uint64_t* bars = reinterpret_cast<uint64_t*>(sKS + 4 * 128);
@@ -200,9 +193,11 @@ sol_fwd_int8p_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_cons
       tma_prefetch_desc(&tm_qi);
       tma_prefetch_desc(&tm_ki);
       tma_prefetch_desc(pv8 ? &tm_vi : &tm_v);
-      mbar_arrive_expect_tx(bar_q, TILE + BOX);
-      for (int i = 0; i < 2; ++i) tma_load_4d(sQ + i * BOX, &tm_q, bar_q, i * 64, u.h, u.qb * BLK, u.b);
-      tma_load_4d(sQI, &tm_qi, bar_q, 0, u.h, u.qb * BLK, u.b);
+      mbar_arrive_expect_tx(bar_q, 2 * TILE);
+      for (int i = 0; i < 2; ++i) {
+        tma_load_4d(sQ + i * BOX, &tm_q, bar_q, i * 64, u.h, u.qb * BLK, u.b);
+        tma_load_4d(sQI + i * BOX, &tm_qi, bar_q, i * 64, u.h, u.qb * BLK, u.b);
+      }
       auto load_k = [&](int stage, int kind, int idx, int jt) {
         uint64_t* bar = bar_kfull + stage;
         uint8_t* dst = sK + stage * TILE;
@@ -210,8 +205,8 @@ sol_fwd_int8p_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_cons
           mbar_arrive_expect_tx(bar, TILE);
           for (int i = 0; i < 2; ++i) tma_load_4d(dst + i * BOX, &tm_kc, bar, i * 64, u.h, idx * 128, u.b);
         } else {
-          mbar_arrive_expect_tx(bar, BOX + BLK * 4);
-          tma_load_4d(dst, &tm_ki, bar, 0, u.h, idx * BLK, u.b);
+          mbar_arrive_expect_tx(bar, TILE + BLK * 4);
+          for (int i = 0; i < 2; ++i) tma_load_4d(dst + i * BOX, &tm_ki, bar, i * 64, u.h, idx * BLK, u.b);
           bulk_load(sKS + (jt & 3) * 128, p.ks + (int64_t)bh * tp + (int64_t)idx * BLK, BLK * 4, bar);
         }
       };
@@ -264,23 +259,19 @@ sol_fwd_int8p_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_cons
       // descriptors of the tile bases; a stage / K-step adds its byte offset >> 4 to
       // the start-address field (shared addresses stay below 2^18: nothing carries)
       const uint64_t qd = make_sw128_desc(smem_u32(sQ), 16, 1024);
-      const uint64_t qid = make_sw128_desc(smem_u32(sQI), 16, 1024);
+      const uint64_t qid = make_sw128_desc(smem_u32(sQI), 16, 1024);   // qi codes, bf16
       const uint64_t kd0 = make_sw128_desc(smem_u32(sK), 16, 1024);
       const uint64_t vd0 = make_sw128_desc(smem_u32(sV), BOX, 1024);   // bf16 V, MN-major
       auto issue_qk = [&](int j, int kind) {
         const int st = j % KST;
         const uint32_t d = tS + (j & 1) * 128;
         const uint64_t kd = kd0 + (uint64_t)(st * (TILE >> 4));
-        if (kind == kTileApprox) {
+        // approximate: bf16 q . kc; exact: the qi codes . the ki codes (both bf16)
+        const uint64_t ad = kind == kTileApprox ? qd : qid;
 #pragma unroll
-          for (int k = 0; k < HD / 16; ++k) {
-            const uint32_t off = ((k >> 2) * BOX + (k & 3) * 32) >> 4;
-            mma_bf16_ss(d, qd + (uint64_t)off, kd + (uint64_t)off, IDESC_QK_BF16, k > 0);
-          }
-        } else {
-#pragma unroll
-          for (int k = 0; k < HD / 32; ++k)
-            mma_i8_ss(d, qid + (uint64_t)(k * 2), kd + (uint64_t)(k * 2), IDESC_QK_I8, k > 0);
+        for (int k = 0; k < HD / 16; ++k) {
+          const uint32_t off = ((k >> 2) * BOX + (k & 3) * 32) >> 4;
+          mma_bf16_ss(d, ad + (uint64_t)off, kd + (uint64_t)off, IDESC_QK_BF16, k > 0);
         }
         tc_commit(bar_kfree + st);
       };
@@ -351,14 +342,16 @@ sol_fwd_int8p_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_cons
       tc_fence_before();
       mbar_arrive(bar_sfree + (j & 1));
       if (ok && exact) {
-        // int32 scores * ks (_int8_fwd.py:329-330); the per-row factor qs * s2 (positive)
+        // exact integer scores (fp32) * ks (_int8_fwd.py:329-330); the per-row factor qs * s2 (positive)
         // is applied to the row max and inside the exponent
         const float4* ks4 = reinterpret_cast<const float4*>(sKS + (j & 3) * 128 + h * 64);
 #pragma unroll
         for (int i = 0; i < 64; i += 4) {
           const float4 k4 = ks4[i >> 2];
-          const float2 s01 = mul2(i2f_exact2(r[i], r[i + 1]), make_float2(k4.x, k4.y));
-          const float2 s23 = mul2(i2f_exact2(r[i + 2], r[i + 3]), make_float2(k4.z, k4.w));
+          const float2 s01 = mul2(make_float2(__uint_as_float(r[i]), __uint_as_float(r[i + 1])),
+                                  make_float2(k4.x, k4.y));
+          const float2 s23 = mul2(make_float2(__uint_as_float(r[i + 2]), __uint_as_float(r[i + 3])),
+                                  make_float2(k4.z, k4.w));
           r[i] = __float_as_uint(s01.x);
           r[i + 1] = __float_as_uint(s01.y);
           r[i + 2] = __float_as_uint(s23.x);
@@ -480,10 +473,10 @@ sol_fwd_int8p_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_cons
   }
 }
 
-// q 32 KB + qi 16 KB + K ring 64 KB + V ring 64 KB + key scales + barriers + mask row +
-// exchange, plus 1 KB to align the tiles to 1024 bytes
+// q 32 KB + qi codes 32 KB + K ring 64 KB + V ring 64 KB + key scales + barriers + mask
+// row + exchange, plus 1 KB to align the tiles to 1024 bytes
 size_t fwd_int8p_smem_bytes() {
-  return (size_t)(2 * 16384 + 16384 + 2 * 32768 + 2 * 32768) + 4 * 128 * 4 + 128 + 4 * kMaskCapI8 +
+  return (size_t)(2 * 32768 + 2 * 32768 + 2 * 32768) + 4 * 128 * 4 + 128 + 4 * kMaskCapI8 +
          4 * (512 + 256) + 16 + 1024;
 }
 

@@ -172,10 +172,12 @@ __global__ void __launch_bounds__(64) pool_kernel(PoolParams p) {
         const float y = __frcp_rn(s_safe);
         if (active) {
           uint32_t c[8];
+          float cv[8];
 #pragma unroll
-          for (int i = 0; i < 8; ++i) c[i] = code_byte(quotient_rn(x[i], s_safe, y));
+          for (int i = 0; i < 8; ++i) c[i] = code_byte_value(quotient_rn(x[i], s_safe, y), cv[i]);
           const int64_t qo = (((int64_t)b * p.T + r) * p.H + h) * HD + d0;
           *reinterpret_cast<uint2*>(p.qi + qo) = pack_codes(c);
+          if (p.qib) *reinterpret_cast<uint4*>(p.qib + qo) = pack8_bf16(cv);
           if (d0 == 0) p.qs[((int64_t)b * p.H + h) * p.tp + r] = s_safe;
         }
       }
@@ -589,6 +591,17 @@ __device__ __forceinline__ uint2 quant8(const float (&x)[8], const float (&den)[
   return pack_codes(c);
 }
 
+// quant8, and the codes as bf16 (exact) packed into `cb`
+__device__ __forceinline__ uint2 quant8_codes(const float (&x)[8], const float (&den)[8], const float (&rcp)[8],
+                                              uint4& cb) {
+  uint32_t c[8];
+  float v[8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) c[i] = code_byte_value(quotient_rn(x[i], den[i], rcp[i]), v[i]);
+  cb = pack8_bf16(v);
+  return pack_codes(c);
+}
+
 // quant8, and the dequantised values bf16(code * den) packed into `deq`
 __device__ __forceinline__ uint2 quant8_deq(const float (&x)[8], const float (&den)[8], const float (&rcp)[8],
                                             uint4& deq) {
@@ -677,10 +690,12 @@ __global__ void __launch_bounds__(256, 3) quant_kv_kernel(QuantParams p) {
       den[c] = s_safe;
       rcp[c] = y;
     }
-    const uint2 qk = quant8(xk, den, rcp);
     const int64_t o = (((int64_t)b * p.T + t) * p.H + h) * HD + d0;
+    uint4 kcb;
+    const uint2 qk = p.kib ? quant8_codes(xk, den, rcp, kcb) : quant8(xk, den, rcp);
     if (ok) {
       *reinterpret_cast<uint2*>(p.ki + o) = qk;
+      if (p.kib) *reinterpret_cast<uint4*>(p.kib + o) = kcb;
       if (d0 == 0) p.ks[((int64_t)b * p.H + h) * p.tp + t] = s_safe;
     }
     if (with_v) {

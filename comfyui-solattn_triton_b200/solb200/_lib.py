@@ -21,7 +21,8 @@ STATUS = {
 
 # enum solb200_buffer
 BUF = dict(error=0, kc=1, vc=2, centroid=3, kmean=4, kvar=5, thr=6, mask=7, count=8, vamax=9,
-           vscale=10, qi=11, qs=12, ki=13, ks=14, vi=15, order=16, vdq=17)
+           vscale=10, qi=11, qs=12, ki=13, ks=14, vi=15, order=16, vdq=17,
+           qib=18, kib=19)
 STAGES_ALL, STAGES_PREPARE, STAGES_FORWARD = 0, 1, 2
 
 _lib = None

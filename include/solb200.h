@@ -78,9 +78,12 @@ enum solb200_buffer {
   SOLB200_BUF_ORDER = 16,     /* int32 [B*H*N] the forward's schedule: unit ids (b*H + h)*N + n,
                                  head by head, each head's query blocks by descending
                                  exact-block count (the cheapest units run last) */
-  SOLB200_BUF_VDQ = 17        /* bf16 [B, T, H, D] dequantised V, vi * vscale rounded to bf16:
+  SOLB200_BUF_VDQ = 17,       /* bf16 [B, T, H, D] dequantised V, vi * vscale rounded to bf16:
                                  the P.V operand of the INT8 forward with int8_pv (head_dim
                                  128, block 128 only; absent otherwise) */
+  SOLB200_BUF_QIB = 18,       /* bf16 [B, T, H, D] the qi codes as bf16 (exact), the Q.K^T
+                                 operand of the INT8 forward (head_dim 128, block 128 only) */
+  SOLB200_BUF_KIB = 19        /* bf16 [B, T, H, D] the ki codes as bf16 (exact), likewise */
 };
 
 /* Thread-local text of the last failure (empty string if none). */
