@@ -67,11 +67,12 @@ __device__ __forceinline__ uint32_t code_byte(float q) {
   return (m ^ sgn) - sgn;
 }
 
-// code_byte(q), and the code as a float in `value`
+// code_byte(q), and the code as a float in `value` (+0 for the code 0: the + 0 turns a
+// -0 from a negative q into +0, as the integer 0 converts)
 __device__ __forceinline__ uint32_t code_byte_value(float q, float& value) {
   const float w = __fadd_rn(fminf(fabsf(q), 127.f), 0.5f);
   const float t = __fadd_rz(w, 8388608.f);   // 2^23 + trunc(w)
-  value = copysignf(__fadd_rn(t, -8388608.f), q);
+  value = __fadd_rn(copysignf(__fadd_rn(t, -8388608.f), q), 0.f);
   const uint32_t m = __float_as_uint(t);
   const uint32_t sgn = (uint32_t)((int32_t)__float_as_uint(q) >> 31);
   return (m ^ sgn) - sgn;
