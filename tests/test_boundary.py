@@ -53,6 +53,24 @@ def test_plan_rejects_bad_geometry(args, code):
     assert _lib.last_error()
 
 
+def test_int8_bf16_operand_buffers_only_for_the_pipelined_shapes():
+    """The bf16 copies of the qi / ki codes and the dequantised V exist for INT8 at head_dim
+    128 with 128-token blocks (the pipelined forward's operands), 3 x 2 bytes per element,
+    and nowhere else."""
+    B, T, H = 1, 4096, 4
+    small = solb200.workspace_bytes(B, T, H, 64, 128, True)
+    big = solb200.workspace_bytes(B, T, H, 128, 128, True)
+    # the three buffers close the plan
+    first = solb200.ops._offset((B, T, H, 128, 128, 1), "vdq")
+    assert big - first >= 3 * 2 * B * T * H * 128
+    n = ctypes.c_int64(0)
+    for which in ("vdq", "qib", "kib"):
+        assert _lib.lib().solb200_workspace_offset(B, T, H, 128, 128, 1, _lib.BUF[which], ctypes.byref(n)) == 0
+        for geom in ((B, T, H, 64, 128, 1), (B, T, H, 128, 64, 1), (B, T, H, 128, 128, 0)):
+            assert _lib.lib().solb200_workspace_offset(*geom, _lib.BUF[which], ctypes.byref(n)) == 1
+    assert small < big
+
+
 def test_offset_of_int8_buffer_in_bf16_workspace_is_an_error():
     n = ctypes.c_int64(0)
     rc = _lib.lib().solb200_workspace_offset(1, 512, 2, 64, 64, 0, _lib.BUF["qi"], ctypes.byref(n))
