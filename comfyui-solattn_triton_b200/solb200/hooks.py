@@ -1,118 +1,167 @@
-"""Model hooks used by the ComfyUI node: Morton reordering of a Wan-style block stack
-and the running block index.
+"""Model hooks for the ComfyUI node: the running block index and the Morton reorder of a
+Wan-style block stack.
 
-    install_wan_morton(model)    _morton.py:85-153: block-0 pre-hook permutes the hidden
-                                 states x[B, T, C] and the RoPE table into Z-order (one
-                                 decision point for both), later blocks reuse the
-                                 permuted table, the last block's post-hook restores the
-                                 token order. Gated on transformer_options["sol_morton"].
-    install_block_index(model)   __init__.py:94-113: publishes transformer_options["sol_block"]
+Behaviour (the reference's, for the host-visible parts):
+  * every block sees ``transformer_options["sol_block"]`` = its position in ``.blocks``
+    (the reference publishes it from per-block pre-hooks, ``__init__.py:94-113``), which the
+    override uses for ``dense_blocks`` and ``tau_profile``;
+  * with ``transformer_options["sol_morton"]`` set, the hidden states ``x [B, T, C]`` and
+    the RoPE table enter the first block in Z-order and leave the last block in the
+    original order (``_morton.py:85-153``), so every attention call in between runs on
+    Morton-ordered tokens.
 
-The permutation and the gathers run on the device (solb200.morton). MiniMax-H3 span
-hooks and the composition with foreign object patches are model-specific glue that
-this build does not provide: the node logs that and Sol-Attn itself still applies.
+Design of this build: one ``_StackHooks`` object per diffusion model, kept in a weak
+registry (nothing is stored on the model). It registers exactly one forward-pre-hook per
+block, which does both jobs, plus one forward hook on the last block. The reorder is a
+small state machine:
+
+    idle --(block 0, flag set, grid matches)--> active(plan) --(last block returns)--> idle
+
+where ``plan`` holds the inverse permutation and the permuted RoPE table for the
+current model call. x and the output are permuted on the device by the row-gather kernel
+(``solb200.permute_tokens``); the small RoPE table by ``index_select``.
+
+MiniMax-H3 span hooks and composition with foreign object patches are model-specific
+glue that this build does not provide: the node logs that and Sol-Attn itself applies.
 """
 
 from __future__ import annotations
 
 import logging
 import math
+import weakref
+from dataclasses import dataclass
 
 import torch
 
 from .morton import morton_perm, permute_tokens
 
-_INSTALLED = set()
-_BLOCK_INDEX = set()
 _logged = set()
 
 
-def _log_once(message):
+def _log_once(message, level=logging.INFO):
     if message not in _logged:
         _logged.add(message)
-        logging.info(f"[sol_attn] {message}")
+        logging.log(level, f"[sol_attn] {message}")
+
+
+@dataclass
+class _Plan:
+    """Reorder plan of one model call."""
+    inverse: torch.Tensor
+    freqs: torch.Tensor
+
+
+def _gather_rows(t: torch.Tensor, index: torch.Tensor) -> torch.Tensor:
+    return permute_tokens(t, index) if t.is_cuda else t.index_select(1, index)
+
+
+class _StackHooks:
+    def __init__(self, model):
+        blocks = getattr(model, "blocks", None)
+        if blocks is None or len(blocks) == 0:
+            raise RuntimeError("block hooks need a non-empty .blocks list on the diffusion model")
+        self.count = len(blocks)
+        self.publish_index = False
+        self.reorder = False
+        self.plan = None
+        for position, block in enumerate(blocks):
+            block.register_forward_pre_hook(self._pre_hook(position), with_kwargs=True)
+        blocks[-1].register_forward_hook(self._after_last, with_kwargs=True)
+
+    # -------------------------------------------------------------- planning
+
+    @staticmethod
+    def _why_not(x, freqs, grid):
+        """None when the call can be reordered, else the reason it cannot."""
+        if grid is None:
+            return "transformer_options has no grid_sizes"
+        tokens = math.prod(int(g) for g in grid)
+        if not (torch.is_tensor(x) and x.dim() == 3 and x.shape[1] == tokens):
+            return f"hidden states do not hold the {tuple(int(g) for g in grid)} video grid"
+        if not (torch.is_tensor(freqs) and freqs.dim() >= 2 and freqs.shape[1] == tokens):
+            return "the RoPE table does not match the video grid"
+        return None
+
+    def _start(self, x, freqs, options):
+        grid = options.get("grid_sizes")
+        reason = self._why_not(x, freqs, grid)
+        if reason is not None:
+            _log_once(f"Wan Morton inactive: {reason}")
+            return None
+        perm, inverse = morton_perm(grid, x.device, options.get("sol_morton_curve", "3d"))
+        xp = _gather_rows(x, perm)
+        fp = freqs.index_select(1, perm.to(freqs.device))   # the RoPE table is small
+        self.plan = _Plan(inverse=inverse, freqs=fp)
+        return xp
+
+    # ----------------------------------------------------------------- hooks
+
+    def _pre_hook(self, position):
+        def hook(_module, args, kwargs):
+            options = kwargs.get("transformer_options")
+            if not isinstance(options, dict):
+                return None
+            if self.publish_index:
+                options["sol_block"] = position
+            if not (self.reorder and options.get("sol_morton") and args):
+                return None
+            if position == 0:
+                self.plan = None   # a new model call starts; drop any unfinished plan
+                xp = self._start(args[0], kwargs.get("freqs"), options)
+                if xp is None:
+                    return None
+                return (xp, *args[1:]), {**kwargs, "freqs": self.plan.freqs}
+            if self.plan is None:
+                return None
+            return args, {**kwargs, "freqs": self.plan.freqs}
+        return hook
+
+    def _after_last(self, _module, _args, _kwargs, output):
+        plan, self.plan = self.plan, None
+        if plan is None:
+            return None
+        if not (torch.is_tensor(output) and output.shape[1] == plan.inverse.numel()):
+            _log_once("Wan Morton: the block stack changed the token count; order not restored",
+                      logging.ERROR)
+            return None
+        return _gather_rows(output, plan.inverse)
+
+
+# Hook objects, keyed by the model's first block (an nn.Module, which supports weak
+# references even when the model object itself does not): they go away with the model.
+_REGISTRY: "weakref.WeakKeyDictionary[object, _StackHooks]" = weakref.WeakKeyDictionary()
+
+
+def _hooks_for(model) -> _StackHooks | None:
+    blocks = getattr(model, "blocks", None)
+    if not blocks:
+        return None
+    key = blocks[0]
+    hooks = _REGISTRY.get(key)
+    if hooks is None:
+        hooks = _StackHooks(model)
+        _REGISTRY[key] = hooks
+    return hooks
 
 
 def install_block_index(model) -> bool:
-    blocks = getattr(model, "blocks", None)
-    if blocks is None:
+    """Publish transformer_options["sol_block"] from every block; False when the model has
+    no .blocks list."""
+    hooks = _hooks_for(model)
+    if hooks is None:
         return False
-    if id(model) in _BLOCK_INDEX:
-        return True
-
-    def make_hook(index):
-        def hook(_module, _args, kwargs):
-            options = kwargs.get("transformer_options")
-            if isinstance(options, dict):
-                options["sol_block"] = index
-            return None
-        return hook
-
-    for index, block in enumerate(blocks):
-        block.register_forward_pre_hook(make_hook(index), with_kwargs=True)
-    _BLOCK_INDEX.add(id(model))
+    hooks.publish_index = True
     return True
 
 
 def install_wan_morton(model):
-    """Idempotently install the reorder hooks; inert without the sol_morton flag."""
-    if id(model) in _INSTALLED:
-        return
-    blocks = getattr(model, "blocks", None)
-    if blocks is None:
+    """Enable the Morton reorder on a Wan-style block stack (inert until the host sets
+    transformer_options["sol_morton"]); idempotent."""
+    hooks = _hooks_for(model)
+    if hooks is None:
         raise RuntimeError("Morton reordering needs .blocks on the diffusion model")
-    first, last = blocks[0], blocks[-1]
-
-    def decide(x, freqs, options):
-        grid = options.get("grid_sizes")
-        if grid is None:
-            _log_once("Wan Morton: transformer_options has no grid_sizes; inactive")
-            return None
-        tokens = int(math.prod(int(g) for g in grid))
-        if not torch.is_tensor(x) or x.ndim != 3 or x.shape[1] != tokens:
-            _log_once(f"Wan Morton: token count does not match the video grid {tuple(grid)}; inactive")
-            return None
-        if not torch.is_tensor(freqs) or freqs.shape[1] != tokens:
-            _log_once("Wan Morton: rope table does not match the video grid; inactive")
-            return None
-        perm, inverse = morton_perm(grid, x.device, options.get("sol_morton_curve", "3d"))
-        return perm, inverse, freqs.index_select(1, perm)
-
-    def pre_hook(module, args, kwargs):
-        options = kwargs.get("transformer_options") or {}
-        if not options.get("sol_morton") or not args:
-            return None
-        if module is first:
-            model._sol_morton_state = None
-            decision = decide(args[0], kwargs.get("freqs"), options)
-            if decision is None:
-                return None
-            perm, inverse, freqs = decision
-            model._sol_morton_state = (perm, inverse, freqs)
-            x = args[0]
-            xp = permute_tokens(x, perm) if x.is_cuda else x.index_select(1, perm)
-            return (xp,) + tuple(args[1:]), {**kwargs, "freqs": freqs}
-        state = getattr(model, "_sol_morton_state", None)
-        if state is None:
-            return None
-        return args, {**kwargs, "freqs": state[2]}
-
-    def post_hook(_module, _args, _kwargs, output):
-        state = getattr(model, "_sol_morton_state", None)
-        if state is None:
-            return None
-        model._sol_morton_state = None
-        inverse = state[1]
-        if not torch.is_tensor(output) or output.shape[1] != inverse.numel():
-            logging.error("[sol_attn] Wan Morton: block stack changed the token count; "
-                          "cannot restore order")
-            return None
-        return permute_tokens(output, inverse) if output.is_cuda else output.index_select(1, inverse)
-
-    for block in blocks:
-        block.register_forward_pre_hook(pre_hook, with_kwargs=True)
-    last.register_forward_hook(post_hook, with_kwargs=True)
-    _INSTALLED.add(id(model))
+    hooks.reorder = True
 
 
 def install_for_model(diffusion_model, morton, sink_conditioning):
