@@ -15,6 +15,14 @@ namespace {
 
 thread_local std::string g_last_error;
 
+// Test hook (solb200_debug_set_wait): the forward kernels' pipeline wait limit and the
+// unit whose CTA stalls on purpose, for calls made from this thread.
+struct DebugWait {
+  uint64_t wait_ns = SOLB200_WAIT_NS;
+  int32_t stall_unit = -1;
+};
+thread_local DebugWait g_debug_wait;
+
 int32_t fail(int32_t code, const std::string& msg) {
   g_last_error = msg;
   return code;
@@ -75,11 +83,6 @@ int32_t make_plan(int64_t B, int64_t T, int64_t H, int64_t D, int32_t blk, int32
     p.off[SOLB200_BUF_VI] = take(B * T * H * D);
   }
   p.off[SOLB200_BUF_ORDER] = take(B * H * p.N * 4);
-  if (p.int8 && D == 128 && blk == 128) {   // operands of the pipelined INT8 forward
-    p.off[SOLB200_BUF_VDQ] = take(B * T * H * D * 2);
-    p.off[SOLB200_BUF_QIB] = take(B * T * H * D * 2);
-    p.off[SOLB200_BUF_KIB] = take(B * T * H * D * 2);
-  }
   p.total = cur;
   return SOLB200_OK;
 }
@@ -209,7 +212,6 @@ int32_t run(const Plan& P, const Call& c) {
   pp.centroid = at<float>(c.ws, P, SOLB200_BUF_CENTROID);
   pp.vamax = (c.int8 && c.int8_pv) ? at<float>(c.ws, P, SOLB200_BUF_VAMAX) : nullptr;
   pp.qi = c.int8 ? at<int8_t>(c.ws, P, SOLB200_BUF_QI) : nullptr;
-  pp.qib = c.int8 && P.off[SOLB200_BUF_QIB] >= 0 ? at<__nv_bfloat16>(c.ws, P, SOLB200_BUF_QIB) : nullptr;
   pp.qs = c.int8 ? at<float>(c.ws, P, SOLB200_BUF_QS) : nullptr;
   pp.B = (int)P.B; pp.T = (int)P.T; pp.H = (int)P.H; pp.N = P.N; pp.npad = P.npad; pp.blk = P.blk;
   pp.tp = P.N * P.blk;
@@ -232,10 +234,8 @@ int32_t run(const Plan& P, const Call& c) {
     qp.kmean = mp.kmean;
     qp.vscale = c.int8_pv ? mp.vscale : nullptr;
     qp.ki = at<int8_t>(c.ws, P, SOLB200_BUF_KI);
-    qp.kib = P.off[SOLB200_BUF_KIB] >= 0 ? at<__nv_bfloat16>(c.ws, P, SOLB200_BUF_KIB) : nullptr;
     qp.ks = at<float>(c.ws, P, SOLB200_BUF_KS);
     qp.vi = c.int8_pv ? at<int8_t>(c.ws, P, SOLB200_BUF_VI) : nullptr;
-    qp.vdq = c.int8_pv && P.off[SOLB200_BUF_VDQ] >= 0 ? at<__nv_bfloat16>(c.ws, P, SOLB200_BUF_VDQ) : nullptr;
     qp.B = (int)P.B; qp.T = (int)P.T; qp.H = (int)P.H; qp.tp = P.N * P.blk;
     launch_quant_kv(qp, hd, c.st);
   }
@@ -270,6 +270,8 @@ int32_t run(const Plan& P, const Call& c) {
   fp.err = err;
   fp.B = (int)P.B; fp.T = (int)P.T; fp.H = (int)P.H; fp.N = P.N; fp.nw = P.nw;
   fp.s2 = s2;
+  fp.wait_ns = g_debug_wait.wait_ns;
+  fp.stall_unit = g_debug_wait.stall_unit;
   FwdMaps m;
   const int64_t npad = P.npad;
   if ((rc = make_map(&m.q, c.q, false, P.D, P.H, P.T, P.B, c.sq[2], c.sq[1], c.sq[0], 128, "q"))) return rc;
@@ -292,24 +294,12 @@ int32_t run(const Plan& P, const Call& c) {
     return SOLB200_OK;
   }
   const int64_t TD = P.H * P.D;
-  if (P.off[SOLB200_BUF_QIB] >= 0) {
-    // the pipelined kernel's Q.K^T operands: the int8 codes as bf16, loaded like q and k
-    if ((rc = make_map(&m.qi, pp.qib, false, P.D, P.H, P.T, P.B, P.D, TD, P.T * TD, 128, "qib"))) return rc;
-    if ((rc = make_map(&m.ki, at<__nv_bfloat16>(c.ws, P, SOLB200_BUF_KIB), false, P.D, P.H, P.T, P.B, P.D, TD,
-                       P.T * TD, kv_rows, "kib")))
-      return rc;
-  } else {
-    if ((rc = make_map(&m.qi, pp.qi, true, P.D, P.H, P.T, P.B, P.D, TD, P.T * TD, 128, "qi"))) return rc;
-    if ((rc = make_map(&m.ki, at<int8_t>(c.ws, P, SOLB200_BUF_KI), true, P.D, P.H, P.T, P.B, P.D, TD, P.T * TD,
-                       P.blk, "ki")))
-      return rc;
-  }
-  if (c.int8_pv && P.off[SOLB200_BUF_VDQ] >= 0) {
-    // the pipelined kernel's P.V operand: bf16 dequantised V, loaded like V
-    if ((rc = make_map(&m.vi, at<__nv_bfloat16>(c.ws, P, SOLB200_BUF_VDQ), false, P.D, P.H, P.T, P.B, P.D, TD,
-                       P.T * TD, kv_rows, "vdq")))
-      return rc;
-  } else if (c.int8_pv) {
+  // int8 operands: qi (128-row query tiles), ki and vi (one routed block per tile)
+  if ((rc = make_map(&m.qi, pp.qi, true, P.D, P.H, P.T, P.B, P.D, TD, P.T * TD, 128, "qi"))) return rc;
+  if ((rc = make_map(&m.ki, at<int8_t>(c.ws, P, SOLB200_BUF_KI), true, P.D, P.H, P.T, P.B, P.D, TD, P.T * TD,
+                     P.blk, "ki")))
+    return rc;
+  if (c.int8_pv) {
     if ((rc = make_map(&m.vi, at<int8_t>(c.ws, P, SOLB200_BUF_VI), true, P.D, P.H, P.T, P.B, P.D, TD,
                        P.T * TD, P.blk, "vi")))
       return rc;
@@ -331,7 +321,7 @@ extern "C" {
 
 const char* solb200_last_error(void) { return g_last_error.c_str(); }
 
-int32_t solb200_abi_version(void) { return 1; }
+int32_t solb200_abi_version(void) { return 2; }
 
 int32_t solb200_workspace_bytes(int64_t batch, int64_t tokens, int64_t heads, int64_t head_dim, int32_t block,
                                 int32_t int8, int64_t* bytes) {
@@ -348,7 +338,7 @@ int32_t solb200_workspace_offset(int64_t batch, int64_t tokens, int64_t heads, i
   Plan p;
   const int32_t rc = make_plan(batch, tokens, heads, head_dim, block, int8, p);
   if (rc) return rc;
-  if (which < 0 || which > SOLB200_BUF_KIB || p.off[which] < 0)
+  if (which < 0 || which > SOLB200_BUF_ORDER || p.off[which] < 0)
     return fail(SOLB200_ERR_INVALID, "buffer not part of this workspace");
   if (!offset) return fail(SOLB200_ERR_INVALID, "offset: null pointer");
   *offset = p.off[which];
@@ -393,6 +383,13 @@ int32_t solb200_sol_attn_int8(const void* q, const int64_t* q_strides, const voi
   return attn_entry(q, q_strides, k, k_strides, v, v_strides, out, batch, tokens, heads, head_dim, block, scale,
                     tau, sink_kv, sink_q, true, int8_pv != 0, stages, workspace, workspace_bytes, lists,
                     route_stat, stream);
+}
+
+int32_t solb200_debug_set_wait(int64_t wait_ns, int32_t stall_unit) {
+  if (stall_unit < -1) return fail(SOLB200_ERR_INVALID, "stall_unit must be -1 (none) or a unit id");
+  g_debug_wait.wait_ns = wait_ns > 0 ? (uint64_t)wait_ns : SOLB200_WAIT_NS;
+  g_debug_wait.stall_unit = stall_unit;
+  return SOLB200_OK;
 }
 
 int32_t solb200_read_device_error(void* workspace, int32_t* code, void* stream) {

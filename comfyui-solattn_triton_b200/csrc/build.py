@@ -21,7 +21,7 @@ PKG = CSRC.parent / "solb200"
 REPO = CSRC.parent.parent
 INCLUDE = REPO / "include"
 OUT = PKG / "libsolb200.so"
-SOURCES = ["prep.cu", "fwd_bf16.cu", "fwd_int8.cu", "fwd_int8p.cu", "api.cu", "noalloc.cu"]
+SOURCES = ["prep.cu", "fwd_bf16.cu", "fwd_int8.cu", "api.cu", "noalloc.cu"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 FLAGS = ["-O3", "-std=c++17", "-lineinfo", "-Xcompiler", "-fPIC", "-Xcompiler", "-fvisibility=hidden",
          "--expt-relaxed-constexpr", f"-I{INCLUDE}", f"-I{CSRC}"]

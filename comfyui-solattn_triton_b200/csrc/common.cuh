@@ -99,13 +99,16 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
 }
 
 // Wait for the phase with the given parity to complete. Bounded: returns false and
-// ORs `code` into *err after SOLB200_WAIT_NS.
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* err, int code) {
+// ORs `code` into *err after `limit_ns` (default SOLB200_WAIT_NS). Kernels pass their
+// launch's pipeline limit for waits inside the pipeline and keep the default for the
+// exit-path drains (which wait only for copies and MMAs already issued).
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* err, int code,
+                                          uint64_t limit_ns = SOLB200_WAIT_NS) {
   if (mbar_try_wait(bar, parity)) return true;
   const uint64_t t0 = globaltimer_ns();
   for (uint32_t it = 1;; ++it) {
     if (mbar_try_wait(bar, parity)) return true;
-    if ((it & 63u) == 0 && globaltimer_ns() - t0 > SOLB200_WAIT_NS) {
+    if ((it & 63u) == 0 && globaltimer_ns() - t0 > limit_ns) {
       if (err) atomicOr(err, code);
       return false;
     }
@@ -115,8 +118,9 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* e
 // Warp-uniform variant for code that continues with warp-collective instructions:
 // every lane polls (bounded), and the warp treats the wait as failed if any lane's
 // wait failed, so lanes never part ways at a later .sync.aligned instruction.
-__device__ __forceinline__ bool mbar_wait_warp(uint64_t* bar, uint32_t parity, int* err, int code) {
-  const bool ok = mbar_wait(bar, parity, err, code);
+__device__ __forceinline__ bool mbar_wait_warp(uint64_t* bar, uint32_t parity, int* err, int code,
+                                               uint64_t limit_ns = SOLB200_WAIT_NS) {
+  const bool ok = mbar_wait(bar, parity, err, code, limit_ns);
   return __all_sync(0xffffffffu, ok) != 0;
 }
 

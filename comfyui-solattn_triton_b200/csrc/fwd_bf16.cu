@@ -55,7 +55,8 @@ sol_fwd_bf16_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_const
   uint64_t* bar_pfull = bars + 7;        // [2]
   uint64_t* bar_pvdone = bars + 9;       // [2]
   uint64_t* bar_drain = bars + 11;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 12);
+  uint64_t* bar_never = bars + 12;       // completed by nothing (the stall_unit test hook)
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 13);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const UnitInfo u = decode_unit(p, blockIdx.x);
@@ -70,6 +71,7 @@ sol_fwd_bf16_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_const
       mbar_init(bar_pvdone + i, 1);
     }
     mbar_init(bar_drain, 1);
+    mbar_init(bar_never, 1);
     fence_barrier_init();
   }
   if (warp == 5) {
@@ -112,12 +114,12 @@ sol_fwd_bf16_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_const
         last_k = sk++;
       }
       for (int s = 0; itv.next(kind, row0); ++s) {
-        if (s >= 2 && !(ok = mbar_wait(bar_pvdone + (s & 1), ((s - 2) >> 1) & 1, p.err, kErrWaitLoad))) break;
+        if (s >= 2 && !(ok = mbar_wait(bar_pvdone + (s & 1), ((s - 2) >> 1) & 1, p.err, kErrWaitLoad, p.wait_ns))) break;
         load_half(s, kind, row0, true);
         last_v = s;
         int kk, kr;
         if (itk.next(kk, kr)) {
-          if (!(ok = mbar_wait(bar_sfull + (s & 1), (s >> 1) & 1, p.err, kErrWaitLoad))) break;
+          if (!(ok = mbar_wait(bar_sfull + (s & 1), (s >> 1) & 1, p.err, kErrWaitLoad, p.wait_ns))) break;
           load_half(s + 2, kk, kr, false);
           last_k = s + 2;
         }
@@ -145,19 +147,20 @@ sol_fwd_bf16_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_const
         }
         tc_commit(bar_sfull + slot);
       };
-      bool ok = mbar_wait(bar_q, 0, p.err, kErrWaitMma);
+      bool ok = mbar_wait(bar_q, 0, p.err, kErrWaitMma, p.wait_ns);
+      if (ok && u.unit == p.stall_unit) ok = mbar_wait(bar_never, 0, p.err, kErrWaitMma, p.wait_ns);
       HalfIter<BLK> itq(p, u), itp(p, u);
       int kind, row0, sq = 0;
       while (ok && sq < 2 && itq.next(kind, row0)) {
-        if (!(ok = mbar_wait(bar_kfull + (sq & 1), (sq >> 1) & 1, p.err, kErrWaitMma))) break;
+        if (!(ok = mbar_wait(bar_kfull + (sq & 1), (sq >> 1) & 1, p.err, kErrWaitMma, p.wait_ns))) break;
         tc_fence_after();
         issue_qk(sq++);
       }
       for (int s = 0; ok && itp.next(kind, row0); ++s) {
         const int slot = s & 1;
         const uint32_t par = (s >> 1) & 1;
-        if (!(ok = mbar_wait(bar_pfull + slot, par, p.err, kErrWaitMma))) break;
-        if (!(ok = mbar_wait(bar_vfull + slot, par, p.err, kErrWaitMma))) break;
+        if (!(ok = mbar_wait(bar_pfull + slot, par, p.err, kErrWaitMma, p.wait_ns))) break;
+        if (!(ok = mbar_wait(bar_vfull + slot, par, p.err, kErrWaitMma, p.wait_ns))) break;
         tc_fence_after();
 #pragma unroll
         for (int kk = 0; kk < 4; ++kk) {
@@ -168,8 +171,8 @@ sol_fwd_bf16_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_const
         tc_commit(bar_pvdone + slot);
         if (itq.next(kind, row0)) {
           // QK(s+2) overwrites slot s's P: let PV(s) finish reading it first
-          if (!(ok = mbar_wait(bar_pvdone + slot, par, p.err, kErrWaitMma))) break;
-          if (!(ok = mbar_wait(bar_kfull + slot, ((s + 2) >> 1) & 1, p.err, kErrWaitMma))) break;
+          if (!(ok = mbar_wait(bar_pvdone + slot, par, p.err, kErrWaitMma, p.wait_ns))) break;
+          if (!(ok = mbar_wait(bar_kfull + slot, ((s + 2) >> 1) & 1, p.err, kErrWaitMma, p.wait_ns))) break;
           tc_fence_after();
           issue_qk(s + 2);
         }
@@ -188,12 +191,12 @@ sol_fwd_bf16_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_const
     bool ok = true;
     for (; it.next(kind, row0); ++s) {
       const int slot = s & 1;
-      if (!(ok = mbar_wait_warp(bar_sfull + slot, (s >> 1) & 1, p.err, kErrWaitSoftmax))) break;
+      if (!(ok = mbar_wait_warp(bar_sfull + slot, (s >> 1) & 1, p.err, kErrWaitSoftmax, p.wait_ns))) break;
       tc_fence_after();
       const uint32_t ts = tS + lane_base + slot * 64;
       // before rescaling O, every P*V issued so far must be complete
       auto drain = [&]() {
-        ok = mbar_wait_warp(bar_pvdone + ((s - 1) & 1), ((s - 1) >> 1) & 1, p.err, kErrWaitSoftmax);
+        ok = mbar_wait_warp(bar_pvdone + ((s - 1) & 1), ((s - 1) >> 1) & 1, p.err, kErrWaitSoftmax, p.wait_ns);
         tc_fence_after();
       };
       uint32_t colmask[2];
@@ -218,7 +221,7 @@ sol_fwd_bf16_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_const
     }
     // epilogue: O / l -> bf16 -> swizzled staging (the free Q buffer) -> TMA store
     if (ok && s > 0 && (ok = mbar_wait_warp(bar_pvdone + ((s - 1) & 1), ((s - 1) >> 1) & 1, p.err,
-                                            kErrWaitEpilogue))) {
+                                            kErrWaitEpilogue, p.wait_ns))) {
       tc_fence_after();
       const float inv = 1.f / l_sum;
       uint8_t* sO = sQ;

@@ -16,6 +16,11 @@ struct FwdParams {
   const float* ks;        // [B, H, T] per-token K scales
   const float* vscale;    // [B, H, D] per-channel V scales (int8 P*V)
   int int8_pv;
+  // bounded waits: limit of the pipeline's waits (the exit-path drains keep the default);
+  // test hook: the CTA running unit `stall_unit` (-1: none) makes its MMA issuer wait on
+  // a barrier that nothing completes, so that its pipeline waits run out
+  uint64_t wait_ns;
+  int stall_unit;
 };
 
 struct FwdMaps {
@@ -24,7 +29,7 @@ struct FwdMaps {
 };
 
 struct UnitInfo {
-  int b, h, qb;
+  int unit, b, h, qb;
   const uint32_t* row;   // this unit's nw mask words: global memory or a shared-memory
                          // copy, so they are read with generic (not ld.global.nc) loads
 };
@@ -36,6 +41,7 @@ struct UnitInfo {
 __device__ __forceinline__ UnitInfo decode_unit(const FwdParams& p, int cta) {
   const int unit = p.order ? __ldg(p.order + cta) : cta;
   UnitInfo u;
+  u.unit = unit;
   u.qb = unit % p.N;
   const int bh = unit / p.N;
   u.b = bh / p.H;
@@ -346,8 +352,6 @@ __device__ __forceinline__ void softmax_half(uint32_t t_s, uint32_t t_o, const u
 
 cudaError_t launch_fwd_bf16(int hd, int blk, const FwdMaps& m, const FwdParams& p, cudaStream_t st);
 cudaError_t launch_fwd_int8(int hd, int blk, const FwdMaps& m, const FwdParams& p, cudaStream_t st);
-// the pipelined INT8 kernel (head_dim 128, 128-token blocks)
-cudaError_t launch_fwd_int8p(const FwdMaps& m, const FwdParams& p, cudaStream_t st);
 size_t fwd_bf16_smem_bytes(int hd);
 
 }  // namespace solb200

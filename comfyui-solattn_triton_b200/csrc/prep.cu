@@ -67,17 +67,6 @@ __device__ __forceinline__ uint32_t code_byte(float q) {
   return (m ^ sgn) - sgn;
 }
 
-// code_byte(q), and the code as a float in `value` (+0 for the code 0: the + 0 turns a
-// -0 from a negative q into +0, as the integer 0 converts)
-__device__ __forceinline__ uint32_t code_byte_value(float q, float& value) {
-  const float w = __fadd_rn(fminf(fabsf(q), 127.f), 0.5f);
-  const float t = __fadd_rz(w, 8388608.f);   // 2^23 + trunc(w)
-  value = __fadd_rn(copysignf(__fadd_rn(t, -8388608.f), q), 0.f);
-  const uint32_t m = __float_as_uint(t);
-  const uint32_t sgn = (uint32_t)((int32_t)__float_as_uint(q) >> 31);
-  return (m ^ sgn) - sgn;
-}
-
 // eight int8 codes (low bytes of c[0..7]) packed into two words, c[0] lowest
 __device__ __forceinline__ uint2 pack_codes(const uint32_t (&c)[8]) {
   uint32_t a, b, lo, hi;
@@ -173,12 +162,10 @@ __global__ void __launch_bounds__(64) pool_kernel(PoolParams p) {
         const float y = __frcp_rn(s_safe);
         if (active) {
           uint32_t c[8];
-          float cv[8];
 #pragma unroll
-          for (int i = 0; i < 8; ++i) c[i] = code_byte_value(quotient_rn(x[i], s_safe, y), cv[i]);
+          for (int i = 0; i < 8; ++i) c[i] = code_byte(quotient_rn(x[i], s_safe, y));
           const int64_t qo = (((int64_t)b * p.T + r) * p.H + h) * HD + d0;
           *reinterpret_cast<uint2*>(p.qi + qo) = pack_codes(c);
-          if (p.qib) *reinterpret_cast<uint4*>(p.qib + qo) = pack8_bf16(cv);
           if (d0 == 0) p.qs[((int64_t)b * p.H + h) * p.tp + r] = s_safe;
         }
       }
@@ -578,8 +565,7 @@ __global__ void __launch_bounds__(256) route_kernel(RouteParams p) {
 
 // K: per-(token, head) int8 of K - k_mean (_fused_quant.py:8-42): s = max|x|/127,
 //    floor 1e-8, round half away from zero of x/s, clamp +-127.
-// V: per-channel int8 with the (b, h, d) scale (_fused_quant.py:61-88); with `vdq` also
-//    the dequantised bf16(code * scale), the pipelined INT8 forward's P.V operand.
+// V: per-channel int8 with the (b, h, d) scale (_fused_quant.py:61-88).
 // One thread per 8 channels of a (head, group of TOK consecutive tokens); a head's lanes
 // share a warp. The K and V rows of all TOK tokens are loaded before any is quantised.
 constexpr int kQuantTok = 2;
@@ -589,31 +575,6 @@ __device__ __forceinline__ uint2 quant8(const float (&x)[8], const float (&den)[
   uint32_t c[8];
 #pragma unroll
   for (int i = 0; i < 8; ++i) c[i] = code_byte(quotient_rn(x[i], den[i], rcp[i]));
-  return pack_codes(c);
-}
-
-// quant8, and the codes as bf16 (exact) packed into `cb`
-__device__ __forceinline__ uint2 quant8_codes(const float (&x)[8], const float (&den)[8], const float (&rcp)[8],
-                                              uint4& cb) {
-  uint32_t c[8];
-  float v[8];
-#pragma unroll
-  for (int i = 0; i < 8; ++i) c[i] = code_byte_value(quotient_rn(x[i], den[i], rcp[i]), v[i]);
-  cb = pack8_bf16(v);
-  return pack_codes(c);
-}
-
-// quant8, and the dequantised values bf16(code * den) packed into `deq`
-__device__ __forceinline__ uint2 quant8_deq(const float (&x)[8], const float (&den)[8], const float (&rcp)[8],
-                                            uint4& deq) {
-  uint32_t c[8];
-  float v[8];
-#pragma unroll
-  for (int i = 0; i < 8; ++i) {
-    c[i] = code_byte_value(quotient_rn(x[i], den[i], rcp[i]), v[i]);
-    v[i] = __fmul_rn(v[i], den[i]);
-  }
-  deq = pack8_bf16(v);
   return pack_codes(c);
 }
 
@@ -692,27 +653,16 @@ __global__ void __launch_bounds__(256, 3) quant_kv_kernel(QuantParams p) {
       rcp[c] = y;
     }
     const int64_t o = (((int64_t)b * p.T + t) * p.H + h) * HD + d0;
-    uint4 kcb;
-    const uint2 qk = p.kib ? quant8_codes(xk, den, rcp, kcb) : quant8(xk, den, rcp);
+    const uint2 qk = quant8(xk, den, rcp);
     if (ok) {
       *reinterpret_cast<uint2*>(p.ki + o) = qk;
-      if (p.kib) *reinterpret_cast<uint4*>(p.kib + o) = kcb;
       if (d0 == 0) p.ks[((int64_t)b * p.H + h) * p.tp + t] = s_safe;
     }
     if (with_v) {
       float xv[8];
       unpack8(uv[i], xv);
-      if (p.vdq) {
-        uint4 dq;
-        const uint2 qv = quant8_deq(xv, sc, sc_rcp, dq);
-        if (ok) {
-          *reinterpret_cast<uint2*>(p.vi + o) = qv;
-          *reinterpret_cast<uint4*>(p.vdq + o) = dq;
-        }
-      } else {
-        const uint2 qv = quant8(xv, sc, sc_rcp);
-        if (ok) *reinterpret_cast<uint2*>(p.vi + o) = qv;
-      }
+      const uint2 qv = quant8(xv, sc, sc_rcp);
+      if (ok) *reinterpret_cast<uint2*>(p.vi + o) = qv;
     }
   }
 }

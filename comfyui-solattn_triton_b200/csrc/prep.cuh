@@ -12,7 +12,6 @@ struct PoolParams {
   float* centroid;                            // [B, N, H, D]
   float* vamax;                               // [B, N, H, D] or null
   int8_t* qi;                                 // [B, T, H, D] or null
-  __nv_bfloat16* qib;                         // [B, T, H, D] the qi codes as bf16, or null
   float* qs;                                  // [B, H, tp] or null
   int B, T, H, N, npad, blk, tp;              // tp = N * blk (row stride of qs)
 };
@@ -48,9 +47,7 @@ struct QuantParams {
   const float* kmean;    // [B, H, D]
   const float* vscale;   // [B, H, D] or null
   int8_t* ki; float* ks; // [B, T, H, D], [B, H, tp]
-  __nv_bfloat16* kib;    // [B, T, H, D] the ki codes as bf16, or null
   int8_t* vi;            // [B, T, H, D] or null
-  __nv_bfloat16* vdq;    // [B, T, H, D] bf16(vi * vscale), or null
   int B, T, H, tp;       // tp = N * blk (row stride of ks)
 };
 

@@ -21,8 +21,7 @@ STATUS = {
 
 # enum solb200_buffer
 BUF = dict(error=0, kc=1, vc=2, centroid=3, kmean=4, kvar=5, thr=6, mask=7, count=8, vamax=9,
-           vscale=10, qi=11, qs=12, ki=13, ks=14, vi=15, order=16, vdq=17,
-           qib=18, kib=19)
+           vscale=10, qi=11, qs=12, ki=13, ks=14, vi=15, order=16)
 STAGES_ALL, STAGES_PREPARE, STAGES_FORWARD = 0, 1, 2
 
 _lib = None
@@ -50,6 +49,8 @@ _SIGS = {
                                                 c_int64, c_int64, c_int32, c_float, c_float,
                                                 POINTER(c_int64), POINTER(c_int64), c_void_p]),
     "solb200_read_device_error": (c_int32, [c_void_p, POINTER(c_int32), c_void_p]),
+    "solb200_noalloc_read_device_error": (c_int32, [POINTER(c_int32), c_void_p]),
+    "solb200_debug_set_wait": (c_int32, [c_int64, c_int32]),
     "solb200_morton_perm": (c_int32, [c_int64, c_int64, c_int64, c_int32, c_int64, c_void_p, c_void_p,
                                       c_void_p]),
     "solb200_copy_heads": (c_int32, [c_void_p, c_void_p, c_int64, c_int64, c_int64, c_int64, c_int64, c_int64,

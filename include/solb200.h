@@ -75,15 +75,9 @@ enum solb200_buffer {
   SOLB200_BUF_KI = 13,        /* int8 [B, T, H, D] (INT8) */
   SOLB200_BUF_KS = 14,        /* fp32 [B, H, N*block] (INT8; entries >= T unused) */
   SOLB200_BUF_VI = 15,        /* int8 [B, T, H, D] (INT8) */
-  SOLB200_BUF_ORDER = 16,     /* int32 [B*H*N] the forward's schedule: unit ids (b*H + h)*N + n,
+  SOLB200_BUF_ORDER = 16      /* int32 [B*H*N] the forward's schedule: unit ids (b*H + h)*N + n,
                                  head by head, each head's query blocks by descending
                                  exact-block count (the cheapest units run last) */
-  SOLB200_BUF_VDQ = 17,       /* bf16 [B, T, H, D] dequantised V, vi * vscale rounded to bf16:
-                                 the P.V operand of the INT8 forward with int8_pv (head_dim
-                                 128, block 128 only; absent otherwise) */
-  SOLB200_BUF_QIB = 18,       /* bf16 [B, T, H, D] the qi codes as bf16 (exact), the Q.K^T
-                                 operand of the INT8 forward (head_dim 128, block 128 only) */
-  SOLB200_BUF_KIB = 19        /* bf16 [B, T, H, D] the ki codes as bf16 (exact), likewise */
 };
 
 /* Thread-local text of the last failure (empty string if none). */
@@ -135,9 +129,13 @@ SOLB200_API int32_t solb200_sol_attn_int8(const void* q, const int64_t* q_stride
  * is a fixed 16 MiB __device__ array inside this library (held on every GPU that loads
  * the library, until exit). The 40-head, 32760-token, head_dim-128 call needs 10.9 MB
  * at 128-token blocks and fits; at 64-token blocks it needs 22.5 MB and, like any call
- * whose solb200_workspace_bytes exceeds 16 MiB, returns SOLB200_ERR_WORKSPACE. The first call on a device looks up the array's address on
- * that device; make it before any stream capture. All calls on a device share the
- * array: calls that overlap on the GPU race and must be serialised by the caller. */
+ * whose solb200_workspace_bytes exceeds 16 MiB, returns SOLB200_ERR_WORKSPACE. The first call
+ * on a device (and the first after the device's context is recreated) looks up the
+ * array's address on that device; make it before any stream capture. All calls on a device
+ * share the array: calls that overlap on the GPU race and must be serialised by the caller.
+ * A bounded-wait timeout inside the call leaves the output unwritten and is recorded in the
+ * array's device error word, which the next call clears: read it after each call with
+ * solb200_noalloc_read_device_error. */
 SOLB200_API int32_t solb200_sol_attn_bf16_noalloc(const void* q, const int64_t* q_strides, const void* k,
                                                   const int64_t* k_strides, const void* v,
                                                   const int64_t* v_strides, void* out, int64_t batch,
@@ -149,6 +147,21 @@ SOLB200_API int32_t solb200_sol_attn_bf16_noalloc(const void* q, const int64_t* 
 /* Synchronise `stream`, read the workspace's device error word into *code and clear
  * it. Returns SOLB200_ERR_TIMEOUT when a kernel recorded a bounded-wait timeout. */
 SOLB200_API int32_t solb200_read_device_error(void* workspace, int32_t* code, void* stream);
+
+/* Test hook for the device-side bounded waits (no counterpart in the reference). For
+ * attention calls made later from the calling thread: the forward kernel's pipeline waits
+ * give up after wait_ns nanoseconds (<= 0: the default, 2 s; the exit-path drains of copies
+ * and MMAs already issued always keep the default), and the CTA that runs unit stall_unit
+ * ((b * heads + h) * N + query block; -1 = none) waits on a barrier that nothing completes,
+ * so that its waits run out: that unit's output is not written, the kernel still returns,
+ * and solb200_read_device_error reports SOLB200_ERR_TIMEOUT. Call (0, -1) to restore. */
+SOLB200_API int32_t solb200_debug_set_wait(int64_t wait_ns, int32_t stall_unit);
+
+/* solb200_read_device_error for the allocation-free entry point: synchronise `stream`,
+ * read the device error word of the current device's static scratch into *code and clear
+ * it (SOLB200_ERR_TIMEOUT when the last solb200_sol_attn_bf16_noalloc call on this device
+ * recorded a bounded-wait timeout). Allocates nothing. No counterpart in the reference. */
+SOLB200_API int32_t solb200_noalloc_read_device_error(int32_t* code, void* stream);
 
 /* Morton (Z-order) permutation of a (frames, height, width) token grid in row-major
  * order: perm[i] = token at position i, inverse[token] = position. curve: 0 = "3d",

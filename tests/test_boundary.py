@@ -27,7 +27,7 @@ def test_library_exports_every_declared_symbol():
     for name in declared:
         assert hasattr(lib, name), f"{name} declared but not exported"
     assert set(declared) == set(_lib.exported_symbols())
-    assert lib.solb200_abi_version() == 1
+    assert lib.solb200_abi_version() == 2
 
 
 def test_workspace_plan_without_gpu():
@@ -53,22 +53,19 @@ def test_plan_rejects_bad_geometry(args, code):
     assert _lib.last_error()
 
 
-def test_int8_bf16_operand_buffers_only_for_the_pipelined_shapes():
-    """The bf16 copies of the qi / ki codes and the dequantised V exist for INT8 at head_dim
-    128 with 128-token blocks (the pipelined forward's operands), 3 x 2 bytes per element,
-    and nowhere else."""
-    B, T, H = 1, 4096, 4
-    small = solb200.workspace_bytes(B, T, H, 64, 128, True)
-    big = solb200.workspace_bytes(B, T, H, 128, 128, True)
-    # the three buffers close the plan
-    first = solb200.ops._offset((B, T, H, 128, 128, 1), "vdq")
-    assert big - first >= 3 * 2 * B * T * H * 128
+def test_int8_workspace_holds_only_int8_operands():
+    """The INT8 workspace holds the int8 codes and their scales, no bf16 copies of them:
+    beyond the BF16 workspace it adds qi, ki, vi (1 byte per element), the per-token Q / K
+    scales, the per-block |V| max and the V scales."""
+    B, T, H, D, blk = 1, 4096, 4, 128, 128
+    bf16 = solb200.workspace_bytes(B, T, H, D, blk, False)
+    int8 = solb200.workspace_bytes(B, T, H, D, blk, True)
+    N = T // blk
+    extra = 3 * B * T * H * D + 2 * 4 * B * H * N * blk + 4 * B * N * H * D + 4 * B * H * D
+    assert int8 - bf16 <= extra + 8 * 256          # plus 256-byte alignment of each buffer
     n = ctypes.c_int64(0)
-    for which in ("vdq", "qib", "kib"):
-        assert _lib.lib().solb200_workspace_offset(B, T, H, 128, 128, 1, _lib.BUF[which], ctypes.byref(n)) == 0
-        for geom in ((B, T, H, 64, 128, 1), (B, T, H, 128, 64, 1), (B, T, H, 128, 128, 0)):
-            assert _lib.lib().solb200_workspace_offset(*geom, _lib.BUF[which], ctypes.byref(n)) == 1
-    assert small < big
+    assert _lib.lib().solb200_workspace_offset(B, T, H, D, blk, 1, 17, ctypes.byref(n)) == 1
+    assert _lib.lib().solb200_abi_version() == 2
 
 
 def test_offset_of_int8_buffer_in_bf16_workspace_is_an_error():

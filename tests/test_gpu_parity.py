@@ -362,25 +362,3 @@ def test_forward_schedule(cuda_device):
         c = counts[seg]
         assert (np.diff(c) <= 0).all(), "query blocks not by descending count"
     assert counts.min() < counts.max(), "fixture should have uneven counts"
-
-
-def test_int8_forward_operands(cuda_device):
-    """The pipelined INT8 forward's bf16 operands (head_dim 128, block 128): the qi / ki
-    codes as bf16 and the dequantised V, bf16(vi * vscale), equal bit for bit to what
-    they are defined as from the bit-exact int8 codes and scales."""
-    from solb200.ops import STAGES_PREPARE, _attn
-    g, (B, T, H, D, blk), (q, k, v) = _golden_inputs("d128")
-    assert D == 128 and blk == 128
-    _, ws, _, _ = _attn(q, k, v, scale=None, tau=float(g["tau"]), sink_blocks=(0, 0), sink_q=(0, 0),
-                        block=blk, int8=True, int8_pv=True, stages=STAGES_PREPARE)
-    qi = ws.view("qi", torch.int8, (B, T, H, D))
-    ki = ws.view("ki", torch.int8, (B, T, H, D))
-    vi = ws.view("vi", torch.int8, (B, T, H, D))
-    vsc = ws.view("vscale", torch.float32, (B, 1, H, D))
-    qib = ws.view("qib", torch.bfloat16, (B, T, H, D))
-    kib = ws.view("kib", torch.bfloat16, (B, T, H, D))
-    vdq = ws.view("vdq", torch.bfloat16, (B, T, H, D))
-    assert torch.equal(qib.view(torch.int16), qi.to(torch.bfloat16).view(torch.int16))
-    assert torch.equal(kib.view(torch.int16), ki.to(torch.bfloat16).view(torch.int16))
-    want = (vi.float() * vsc).to(torch.bfloat16)
-    assert torch.equal(vdq.view(torch.int16), want.view(torch.int16))

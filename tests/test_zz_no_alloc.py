@@ -7,8 +7,9 @@ device synchronisation. Its scratch is a fixed 16 MiB array inside the library, 
 by every call on a device, so these tests check that two calls in a row (different
 shapes, so the second starts from the first call's leftovers) each give the same
 result as ``solb200_sol_attn_bf16`` with a caller workspace, within the parity
-tolerance of the other GPU tests, and that a call whose scratch would not fit is
-refused with a workspace error.
+tolerance of the other GPU tests, with no bounded-wait timeout recorded in the scratch's
+device error word (read after every call), and that a call whose scratch would not fit
+is refused with a workspace error.
 
 The file sorts last so that it also runs after every other GPU test in one process;
 it must pass alone in a fresh process too, where its first call does the per-device
@@ -47,7 +48,18 @@ def _noalloc(q, k, v, *, tau, block, scale=None, sink_blocks=(0, 0), sink_q=(0, 
         out.data_ptr(), B, T, H, D, block, scale, tau, (c_int64 * 2)(*sink_blocks),
         (c_int64 * 2)(*sink_q), torch.cuda.current_stream().cuda_stream)
     check(rc, "sol_attn_bf16_noalloc")
+    _assert_no_device_error()
     return out
+
+
+def _assert_no_device_error():
+    """The call's device error word (in the static scratch) records no bounded-wait
+    timeout; reading it synchronises the stream and clears it."""
+    code = ctypes.c_int32(-1)
+    rc = lib().solb200_noalloc_read_device_error(ctypes.byref(code),
+                                                 torch.cuda.current_stream().cuda_stream)
+    check(rc, "noalloc_read_device_error")
+    assert code.value == 0
 
 
 def _assert_close(got, want, label):
