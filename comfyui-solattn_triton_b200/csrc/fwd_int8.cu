@@ -11,15 +11,17 @@
 //     INT8 P.V (int8_pv, :336-353): bm = the block's row max, pe = 2^(s - bm),
 //       beta = 2^(bm - m), l = l alpha + beta sum(pe), pi = trunc(min(pe*127 + 0.5, 127))
 //       (int8 codes in shared memory), PV = pi . vi on kind::i8 into int32 TMEM, folded
-//       by the softmax threads: O = O alpha + fp32(PV) * ((beta / 127) * vscale[d]).
+//       by the softmax threads: O = O alpha + fp32(PV) * ((beta / 127) * vscale[d]) (vscale
+//       applied in the epilogue, see below).
 //     BF16 P.V: P = 2^(s - m) in bf16 (TMEM) . V (bf16) on kind::f16 into O.
 // The online softmax keeps a per-row reference max m that is raised only when a tile
 // exceeds it by more than 2^8 (then O and l are rescaled by alpha = 2^(m_old - m_new));
 // the int8 codes are relative to each block's own max, so they do not depend on it.
 //
-// int32 -> fp32 conversions (scores and P.V) are exact magic-number additions on the
-// FMA pipe: |acc| <= 127^2 * head_dim < 2^22, so the bits 0x4B400000 + acc are the float
-// 1.5 * 2^23 + acc, and subtracting 1.5 * 2^23 leaves acc exactly.
+// int32 -> fp32 conversions (scores and P.V) are exact: |acc| <= 127^2 * head_dim < 2^24.
+// Folded int8 P.V products are accumulated in units of vscale[d] (fp32(PV) * beta / 127),
+// the epilogue multiplies by vscale[d] (an approximate-tile contribution made before the
+// first fold is divided by vscale[d] once).
 //
 // One CTA per unit, 192 threads: warps 0-3 softmax + fold + epilogue (thread = query row
 // = TMEM lane), warp 4 TMA producer, warp 5 TMEM allocator + MMA issuer. Two CTAs share
@@ -55,12 +57,6 @@ __device__ __forceinline__ uint32_t swz_off(int r, int c, int rb) {
   return rb == 128 ? (uint32_t)(r * 128 + ((c ^ (r & 7)) << 4)) : (uint32_t)(r * 64 + ((c ^ ((r >> 1) & 3)) << 4));
 }
 
-// Two int32 (as raw bits) to fp32, exactly, for |a|, |b| < 2^22.
-__device__ __forceinline__ float2 i2f2(uint32_t a, uint32_t b) {
-  const float2 x = make_float2(__uint_as_float(a + 0x4B400000u), __uint_as_float(b + 0x4B400000u));
-  return add2(x, make_float2(-12582912.f, -12582912.f));
-}
-
 __device__ __forceinline__ float2 add_rz2(float2 a, float2 b) {
   uint64_t r;
   asm("add.rz.f32x2 %0, %1, %2;"
@@ -93,19 +89,19 @@ __device__ __forceinline__ float max_n(const uint32_t (&r)[N]) {
   return max3(m4[0], m4[1], fmaxf(m4[2], m4[3]));
 }
 
-// Exact-tile scores of this row: r[i] (int32 bits) <- fp32(acc_i) * (qs_log2 * ks_i)
-// (_int8_fwd.py:330), tokens at or past `valid` set to -inf when MASKED.
+// Exact-tile scores of this row without the row factor: r[i] (int32 bits) <- fp32(acc_i) *
+// ks_i, tokens at or past `valid` set to -inf when MASKED. The row factor qs * s2 (> 0, or
+// 0 past T) multiplies the row max and enters the exponent's FMA; the reference multiplies
+// acc by qs * s2 * ks at once (_int8_fwd.py:330): the two orders differ in the last bit.
 template <int BLK, bool MASKED>
-__device__ __forceinline__ void exact_scores(uint32_t (&r)[BLK], const float* __restrict__ ks, float qs_log2,
-                                             int valid) {
-  const float2 qv = make_float2(qs_log2, qs_log2);
+__device__ __forceinline__ void exact_scores(uint32_t (&r)[BLK], const float* __restrict__ ks, int valid) {
 #pragma unroll
   for (int i = 0; i < BLK; i += 4) {
     const float4 k4 = *reinterpret_cast<const float4*>(ks + i);
-    const float2 c01 = mul2(qv, make_float2(k4.x, k4.y));
-    const float2 c23 = mul2(qv, make_float2(k4.z, k4.w));
-    const float2 s01 = mul2(i2f2(r[i], r[i + 1]), c01);
-    const float2 s23 = mul2(i2f2(r[i + 2], r[i + 3]), c23);
+    const float2 s01 = mul2(make_float2(__int2float_rn((int)r[i]), __int2float_rn((int)r[i + 1])),
+                            make_float2(k4.x, k4.y));
+    const float2 s23 = mul2(make_float2(__int2float_rn((int)r[i + 2]), __int2float_rn((int)r[i + 3])),
+                            make_float2(k4.z, k4.w));
     r[i] = __float_as_uint(s01.x);
     r[i + 1] = __float_as_uint(s01.y);
     r[i + 2] = __float_as_uint(s23.x);
@@ -118,15 +114,15 @@ __device__ __forceinline__ void exact_scores(uint32_t (&r)[BLK], const float* __
   }
 }
 
-// P = 2^(s - m) as bf16 pairs written over r[0 .. BLK/2) (pair k = columns 2k, 2k+1);
+// P = 2^(t * sc - m) as bf16 pairs written over r[0 .. BLK/2) (pair k = columns 2k, 2k+1);
 // returns the row sum.
 template <int BLK>
-__device__ __forceinline__ float exp_bf16(uint32_t (&r)[BLK], float m) {
-  const float2 nm = make_float2(-m, -m);
+__device__ __forceinline__ float exp_bf16(uint32_t (&r)[BLK], float sc, float m) {
+  const float2 nm = make_float2(-m, -m), scv = make_float2(sc, sc);
   float2 acc[4] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
 #pragma unroll
   for (int i = 0; i < BLK; i += 2) {
-    const float2 x = add2(make_float2(__uint_as_float(r[i]), __uint_as_float(r[i + 1])), nm);
+    const float2 x = fma2(make_float2(__uint_as_float(r[i]), __uint_as_float(r[i + 1])), scv, nm);
     const float2 p = make_float2(fast_exp2(x.x), fast_exp2(x.y));
     acc[(i >> 1) & 3] = add2(acc[(i >> 1) & 3], p);
     r[i >> 1] = pack_bf16x2(p.x, p.y);
@@ -140,8 +136,8 @@ __device__ __forceinline__ float exp_bf16(uint32_t (&r)[BLK], float m) {
 // 127.5, both steps rounded as the reference's), written to the swizzled K-major P tile
 // in shared memory; returns sum(pe).
 template <int BLK>
-__device__ __forceinline__ float exp_codes(const uint32_t (&r)[BLK], float bm, uint8_t* sP, int row) {
-  const float2 nbm = make_float2(-bm, -bm), k127 = make_float2(127.f, 127.f);
+__device__ __forceinline__ float exp_codes(const uint32_t (&r)[BLK], float sc, float bm, uint8_t* sP, int row) {
+  const float2 nbm = make_float2(-bm, -bm), k127 = make_float2(127.f, 127.f), scv = make_float2(sc, sc);
   const float2 half = make_float2(0.5f, 0.5f), big = make_float2(8388608.f, 8388608.f);
   float2 acc[4] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
 #pragma unroll
@@ -153,10 +149,10 @@ __device__ __forceinline__ float exp_codes(const uint32_t (&r)[BLK], float bm, u
 #pragma unroll
       for (int e = 0; e < 2; ++e) {
         const int i = c * 16 + q * 4 + e * 2;
-        const float2 x = add2(make_float2(__uint_as_float(r[i]), __uint_as_float(r[i + 1])), nbm);
+        const float2 x = fma2(make_float2(__uint_as_float(r[i]), __uint_as_float(r[i + 1])), scv, nbm);
         const float2 pe = make_float2(fast_exp2(x.x), fast_exp2(x.y));
         acc[(q + e) & 3] = add2(acc[(q + e) & 3], pe);
-        const float2 t = add_rz2(add2(mul2(pe, k127), half), big);
+        const float2 t = add_rz2(fma2(pe, k127, half), big);
         code[2 * e] = __float_as_uint(t.x);
         code[2 * e + 1] = __float_as_uint(t.y);
       }
@@ -168,10 +164,11 @@ __device__ __forceinline__ float exp_codes(const uint32_t (&r)[BLK], float bm, u
   return a.x + a.y;
 }
 
-// O += fp32(PV) * (f * vscale[d]) over this row's HD columns of O in TMEM (PV int32 in
-// the S columns); with LIVE false, O = fp32(PV) * (f * vscale[d]).
+// O += fp32(PV) * f over this row's HD columns of O in TMEM (PV int32 in the S columns),
+// O in units of vscale[d] (the epilogue multiplies by vscale[d]); with LIVE false,
+// O = fp32(PV) * f.
 template <int HD, bool LIVE>
-__device__ __forceinline__ void fold_pv(uint32_t t_pv, uint32_t t_o, float f, const float* __restrict__ vsc) {
+__device__ __forceinline__ void fold_pv(uint32_t t_pv, uint32_t t_o, float f) {
   const float2 f2 = make_float2(f, f);
 #pragma unroll 1
   for (int c = 0; c < HD / 32; ++c) {
@@ -180,26 +177,30 @@ __device__ __forceinline__ void fold_pv(uint32_t t_pv, uint32_t t_o, float f, co
     if (LIVE) tmem_ld32(t_o + c * 32, o);
     tmem_wait_ld();
 #pragma unroll
-    for (int i = 0; i < 32; i += 4) {
-      const float4 v4 = *reinterpret_cast<const float4*>(vsc + c * 32 + i);
-      const float2 g01 = mul2(f2, make_float2(v4.x, v4.y));
-      const float2 g23 = mul2(f2, make_float2(v4.z, v4.w));
-      const float2 p01 = i2f2(pv[i], pv[i + 1]), p23 = i2f2(pv[i + 2], pv[i + 3]);
-      float2 o01, o23;
-      if (LIVE) {
-        o01 = fma2(p01, g01, make_float2(__uint_as_float(o[i]), __uint_as_float(o[i + 1])));
-        o23 = fma2(p23, g23, make_float2(__uint_as_float(o[i + 2]), __uint_as_float(o[i + 3])));
-      } else {
-        o01 = mul2(p01, g01);
-        o23 = mul2(p23, g23);
-      }
-      o[i] = __float_as_uint(o01.x);
-      o[i + 1] = __float_as_uint(o01.y);
-      o[i + 2] = __float_as_uint(o23.x);
-      o[i + 3] = __float_as_uint(o23.y);
+    for (int i = 0; i < 32; i += 2) {
+      const float2 pf = make_float2(__int2float_rn((int)pv[i]), __int2float_rn((int)pv[i + 1]));
+      const float2 v = LIVE ? fma2(pf, f2, make_float2(__uint_as_float(o[i]), __uint_as_float(o[i + 1])))
+                            : mul2(pf, f2);
+      o[i] = __float_as_uint(v.x);
+      o[i + 1] = __float_as_uint(v.y);
     }
     tmem_st32(t_o + c * 32, o);
   }
+}
+
+// O[d] /= vscale[d] over this row's HD columns (O from true units to units of vscale[d]).
+template <int HD>
+__device__ __forceinline__ void to_vscale_units(uint32_t t_o, const float* __restrict__ vsc) {
+#pragma unroll 1
+  for (int c = 0; c < HD / 32; ++c) {
+    uint32_t o[32];
+    tmem_ld32(t_o + c * 32, o);
+    tmem_wait_ld();
+#pragma unroll
+    for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__fdiv_rn(__uint_as_float(o[i]), vsc[c * 32 + i]));
+    tmem_st32(t_o + c * 32, o);
+  }
+  tmem_wait_st();
 }
 
 }  // namespace
@@ -431,6 +432,7 @@ sol_fwd_int8_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_const
     int j = 0, e = -1, kind, idx;
     bool ok = mbar_wait_warp(bar_q, 0, p.err, kErrWaitSoftmax, p.wait_ns);   // vscale is staged with q
     bool last_fold = false;
+    bool o_scaled = false;   // O holds units of vscale[d] (int8 P.V folds; see fold_pv)
     for (; ok && it.next(kind, idx); ++j) {
       const bool exact = kind == kTileExact;
       if (exact) ++e;
@@ -458,9 +460,9 @@ sol_fwd_int8_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_const
       tmem_wait_ld();
       const int valid = p.T - idx * BLK;
       const float* ks = sKS + (e & 3) * BLK;
-      if (valid < BLK) exact_scores<BLK, true>(r, ks, qs_log2, valid);
-      else exact_scores<BLK, false>(r, ks, qs_log2, valid);
-      const float bm = max_n<BLK>(r);
+      if (valid < BLK) exact_scores<BLK, true>(r, ks, valid);
+      else exact_scores<BLK, false>(r, ks, valid);
+      const float bm = max_n<BLK>(r) * qs_log2;   // the block's row max (log2 units)
       const float m_new = fmaxf(m_ref, bm);
       float alpha = 1.f;
       bool need = false;
@@ -478,7 +480,7 @@ sol_fwd_int8_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_const
         rescale_rows<HD>(tO + lane_base, alpha);
       }
       if (!pv8) {
-        l_sum += exp_bf16<BLK>(r, m_ref);
+        l_sum += exp_bf16<BLK>(r, qs_log2, m_ref);
 #pragma unroll
         for (int c = 0; c < BLK / 32; ++c)
           tmem_st16(ts + c * 16, *reinterpret_cast<const uint32_t(*)[16]>(&r[c * 16]));
@@ -490,7 +492,7 @@ sol_fwd_int8_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_const
       }
       // int8 P.V: codes to shared memory, then fold the tensor core's int32 product
       const float beta = fast_exp2(bm - m_ref);
-      const float psum = exp_codes<BLK>(r, bm, sP, row);
+      const float psum = exp_codes<BLK>(r, qs_log2, bm, sP, row);
       l_sum = l_sum + beta * psum;
       fence_proxy_async_smem();   // P (generic stores) -> tensor core (async proxy)
       tc_fence_before();
@@ -498,8 +500,10 @@ sol_fwd_int8_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_const
       if (!(ok = mbar_wait_warp(bar_pvdone, j & 1, p.err, kErrWaitSoftmax, p.wait_ns))) break;
       tc_fence_after();
       const float f = beta * (1.0f / 127.0f);
-      if (o_live) fold_pv<HD, true>(ts, tO + lane_base, f, sVSC);
-      else fold_pv<HD, false>(ts, tO + lane_base, f, sVSC);
+      if (o_live && !o_scaled) to_vscale_units<HD>(tO + lane_base, sVSC);   // after approximate tiles
+      if (o_live) fold_pv<HD, true>(ts, tO + lane_base, f);
+      else fold_pv<HD, false>(ts, tO + lane_base, f);
+      o_scaled = true;
       tmem_wait_st();
       tc_fence_before();
       mbar_arrive(bar_sfree);
@@ -521,11 +525,14 @@ sol_fwd_int8_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_const
           const int col_byte0 = ((c * 32) % 64) * 2;
 #pragma unroll
           for (int v4 = 0; v4 < 4; ++v4) {
+            float sc[8];
+#pragma unroll
+            for (int t = 0; t < 8; ++t) sc[t] = o_scaled ? inv * sVSC[c * 32 + v4 * 8 + t] : inv;
             uint4 w;
-            w.x = pack_bf16x2(__uint_as_float(o[v4 * 8 + 0]) * inv, __uint_as_float(o[v4 * 8 + 1]) * inv);
-            w.y = pack_bf16x2(__uint_as_float(o[v4 * 8 + 2]) * inv, __uint_as_float(o[v4 * 8 + 3]) * inv);
-            w.z = pack_bf16x2(__uint_as_float(o[v4 * 8 + 4]) * inv, __uint_as_float(o[v4 * 8 + 5]) * inv);
-            w.w = pack_bf16x2(__uint_as_float(o[v4 * 8 + 6]) * inv, __uint_as_float(o[v4 * 8 + 7]) * inv);
+            w.x = pack_bf16x2(__uint_as_float(o[v4 * 8 + 0]) * sc[0], __uint_as_float(o[v4 * 8 + 1]) * sc[1]);
+            w.y = pack_bf16x2(__uint_as_float(o[v4 * 8 + 2]) * sc[2], __uint_as_float(o[v4 * 8 + 3]) * sc[3]);
+            w.z = pack_bf16x2(__uint_as_float(o[v4 * 8 + 4]) * sc[4], __uint_as_float(o[v4 * 8 + 5]) * sc[5]);
+            w.w = pack_bf16x2(__uint_as_float(o[v4 * 8 + 6]) * sc[6], __uint_as_float(o[v4 * 8 + 7]) * sc[7]);
             const int chunk = (col_byte0 >> 4) + v4;
             *reinterpret_cast<uint4*>(sO + box * (BLK * 128) + row * 128 + ((chunk ^ (row & 7)) << 4)) = w;
           }
