@@ -43,6 +43,9 @@ struct Plan {
   bool int8;
   int64_t off[20];
   int64_t total;
+  // reordered calls: dense copies of q / k / v in the call's token order (offsets, -1 if
+  // the path does not read that tensor by tiles), after every other buffer
+  int64_t off_copy[3];
 };
 
 int64_t align_up(int64_t x, int64_t a) { return (x + a - 1) / a * a; }
@@ -84,6 +87,22 @@ int32_t make_plan(int64_t B, int64_t T, int64_t H, int64_t D, int32_t blk, int32
   }
   p.off[SOLB200_BUF_ORDER] = take(B * H * p.N * 4);
   p.total = cur;
+  p.off_copy[0] = p.off_copy[1] = p.off_copy[2] = -1;
+  return SOLB200_OK;
+}
+
+// The plan of a reordered call: the forward reads q (both paths), k (BF16) and v (BF16, or
+// INT8 without int8 P.V) by TMA tiles, so those are copied in the call's token order.
+int32_t make_plan_reordered(int64_t B, int64_t T, int64_t H, int64_t D, int32_t blk, int32_t int8, int32_t int8_pv,
+                            Plan& p) {
+  const int32_t rc = make_plan(B, T, H, D, blk, int8, p);
+  if (rc) return rc;
+  const bool need[3] = {true, !p.int8, !p.int8 || !int8_pv};
+  for (int i = 0; i < 3; ++i) {
+    if (!need[i]) continue;
+    p.off_copy[i] = p.total;
+    p.total = align_up(p.total + B * T * H * D * 2, 256);
+  }
   return SOLB200_OK;
 }
 
@@ -175,6 +194,7 @@ struct Call {
   int64_t ws_bytes;
   int32_t* lists;
   float* stat;
+  const int64_t* perm;   // token order of a reordered call, or null
   cudaStream_t st;
 };
 
@@ -213,6 +233,13 @@ int32_t run(const Plan& P, const Call& c) {
   pp.vamax = (c.int8 && c.int8_pv) ? at<float>(c.ws, P, SOLB200_BUF_VAMAX) : nullptr;
   pp.qi = c.int8 ? at<int8_t>(c.ws, P, SOLB200_BUF_QI) : nullptr;
   pp.qs = c.int8 ? at<float>(c.ws, P, SOLB200_BUF_QS) : nullptr;
+  pp.perm = c.perm;
+  pp.err = err;
+  __nv_bfloat16* copies[3] = {nullptr, nullptr, nullptr};
+  for (int i = 0; i < 3; ++i)
+    if (c.perm && P.off_copy[i] >= 0)
+      copies[i] = reinterpret_cast<__nv_bfloat16*>(static_cast<char*>(c.ws) + P.off_copy[i]);
+  pp.qcopy = copies[0]; pp.kcopy = copies[1]; pp.vcopy = copies[2];
   pp.B = (int)P.B; pp.T = (int)P.T; pp.H = (int)P.H; pp.N = P.N; pp.npad = P.npad; pp.blk = P.blk;
   pp.tp = P.N * P.blk;
   if (prep) launch_pool(pp, hd, pp.vamax != nullptr, c.int8, c.st);
@@ -237,6 +264,8 @@ int32_t run(const Plan& P, const Call& c) {
     qp.ks = at<float>(c.ws, P, SOLB200_BUF_KS);
     qp.vi = c.int8_pv ? at<int8_t>(c.ws, P, SOLB200_BUF_VI) : nullptr;
     qp.B = (int)P.B; qp.T = (int)P.T; qp.H = (int)P.H; qp.tp = P.N * P.blk;
+    qp.perm = c.perm;
+    qp.err = err;
     launch_quant_kv(qp, hd, c.st);
   }
 
@@ -272,9 +301,20 @@ int32_t run(const Plan& P, const Call& c) {
   fp.s2 = s2;
   fp.wait_ns = g_debug_wait.wait_ns;
   fp.stall_unit = g_debug_wait.stall_unit;
+  fp.perm = c.perm;
+  fp.out = static_cast<__nv_bfloat16*>(c.out);
   FwdMaps m;
   const int64_t npad = P.npad;
-  if ((rc = make_map(&m.q, c.q, false, P.D, P.H, P.T, P.B, c.sq[2], c.sq[1], c.sq[0], 128, "q"))) return rc;
+  // reordered calls read the dense copies in the call's token order
+  const int64_t TD = P.H * P.D;
+  const int64_t dense_s[3] = {TD * P.T, TD, P.D};
+  const void* qsrc = copies[0] ? copies[0] : c.q;
+  const void* ksrc = copies[1] ? copies[1] : c.k;
+  const void* vsrc = copies[2] ? copies[2] : c.v;
+  const int64_t* sqm = copies[0] ? dense_s : c.sq;
+  const int64_t* skm = copies[1] ? dense_s : c.sk;
+  const int64_t* svm = copies[2] ? dense_s : c.sv;
+  if ((rc = make_map(&m.q, qsrc, false, P.D, P.H, P.T, P.B, sqm[2], sqm[1], sqm[0], 128, "q"))) return rc;
   // the BF16 kernel streams 64-row halves; the INT8 kernel 128-row pooled chunks
   const int pooled_rows = c.int8 ? 128 : 64;
   const int kv_rows = c.int8 ? P.blk : 64;
@@ -287,13 +327,12 @@ int32_t run(const Plan& P, const Call& c) {
   if ((rc = make_map(&m.o, c.out, false, P.D, P.H, P.T, P.B, P.D, P.H * P.D, P.T * P.H * P.D, P.blk, "out")))
     return rc;
   if (!c.int8) {
-    if ((rc = make_map(&m.k, c.k, false, P.D, P.H, P.T, P.B, c.sk[2], c.sk[1], c.sk[0], kv_rows, "k"))) return rc;
-    if ((rc = make_map(&m.v, c.v, false, P.D, P.H, P.T, P.B, c.sv[2], c.sv[1], c.sv[0], kv_rows, "v"))) return rc;
+    if ((rc = make_map(&m.k, ksrc, false, P.D, P.H, P.T, P.B, skm[2], skm[1], skm[0], kv_rows, "k"))) return rc;
+    if ((rc = make_map(&m.v, vsrc, false, P.D, P.H, P.T, P.B, svm[2], svm[1], svm[0], kv_rows, "v"))) return rc;
     e = launch_fwd_bf16(hd, P.blk, m, fp, c.st);
     if (e != cudaSuccess) return cuda_fail(e, "bf16 forward launch");
     return SOLB200_OK;
   }
-  const int64_t TD = P.H * P.D;
   // int8 operands: qi (128-row query tiles), ki and vi (one routed block per tile)
   if ((rc = make_map(&m.qi, pp.qi, true, P.D, P.H, P.T, P.B, P.D, TD, P.T * TD, 128, "qi"))) return rc;
   if ((rc = make_map(&m.ki, at<int8_t>(c.ws, P, SOLB200_BUF_KI), true, P.D, P.H, P.T, P.B, P.D, TD, P.T * TD,
@@ -304,7 +343,7 @@ int32_t run(const Plan& P, const Call& c) {
                        P.T * TD, P.blk, "vi")))
       return rc;
   } else {
-    if ((rc = make_map(&m.v, c.v, false, P.D, P.H, P.T, P.B, c.sv[2], c.sv[1], c.sv[0], kv_rows, "v"))) return rc;
+    if ((rc = make_map(&m.v, vsrc, false, P.D, P.H, P.T, P.B, svm[2], svm[1], svm[0], kv_rows, "v"))) return rc;
   }
   fp.qs = pp.qs;
   fp.ks = at<float>(c.ws, P, SOLB200_BUF_KS);
@@ -349,9 +388,10 @@ static int32_t attn_entry(const void* q, const int64_t* sq, const void* k, const
                           const int64_t* sv, void* out, int64_t B, int64_t T, int64_t H, int64_t D, int32_t blk,
                           float scale, float tau, const int64_t* sink_kv, const int64_t* sink_q, bool int8,
                           bool int8_pv, int32_t stages, void* ws, int64_t ws_bytes, int32_t* lists, float* stat,
-                          void* stream) {
+                          void* stream, const int64_t* perm = nullptr) {
   Plan P;
-  int32_t rc = make_plan(B, T, H, D, blk, int8 ? 1 : 0, P);
+  int32_t rc = perm ? make_plan_reordered(B, T, H, D, blk, int8 ? 1 : 0, int8_pv ? 1 : 0, P)
+                    : make_plan(B, T, H, D, blk, int8 ? 1 : 0, P);
   if (rc) return rc;
   Call c{};
   c.q = q; c.k = k; c.v = v; c.sq = sq; c.sk = sk; c.sv = sv; c.out = out;
@@ -359,7 +399,7 @@ static int32_t attn_entry(const void* q, const int64_t* sq, const void* k, const
   c.sink_kv[0] = sink_kv ? sink_kv[0] : 0; c.sink_kv[1] = sink_kv ? sink_kv[1] : 0;
   c.sink_q[0] = sink_q ? sink_q[0] : 0; c.sink_q[1] = sink_q ? sink_q[1] : 0;
   c.stages = stages; c.int8 = int8; c.int8_pv = int8_pv;
-  c.ws = ws; c.ws_bytes = ws_bytes; c.lists = lists; c.stat = stat;
+  c.ws = ws; c.ws_bytes = ws_bytes; c.lists = lists; c.stat = stat; c.perm = perm;
   c.st = static_cast<cudaStream_t>(stream);
   return run(P, c);
 }
@@ -385,6 +425,28 @@ int32_t solb200_sol_attn_int8(const void* q, const int64_t* q_strides, const voi
                     route_stat, stream);
 }
 
+int32_t solb200_workspace_bytes_reordered(int64_t batch, int64_t tokens, int64_t heads, int64_t head_dim,
+                                          int32_t block, int32_t int8, int32_t int8_pv, int64_t* bytes) {
+  Plan p;
+  const int32_t rc = make_plan_reordered(batch, tokens, heads, head_dim, block, int8, int8_pv, p);
+  if (rc) return rc;
+  if (!bytes) return fail(SOLB200_ERR_INVALID, "bytes: null pointer");
+  *bytes = p.total;
+  return SOLB200_OK;
+}
+
+int32_t solb200_sol_attn_reordered(const void* q, const int64_t* q_strides, const void* k, const int64_t* k_strides,
+                                   const void* v, const int64_t* v_strides, void* out, int64_t batch, int64_t tokens,
+                                   int64_t heads, int64_t head_dim, int32_t block, float scale, float tau,
+                                   const int64_t* sink_kv, const int64_t* sink_q, const int64_t* order, int32_t int8,
+                                   int32_t int8_pv, void* workspace, int64_t workspace_bytes, void* stream) {
+  if (!order) return fail(SOLB200_ERR_INVALID, "order: null pointer");
+  if (reinterpret_cast<uintptr_t>(order) & 7u) return fail(SOLB200_ERR_ALIGNMENT, "order: not 8-byte aligned");
+  return attn_entry(q, q_strides, k, k_strides, v, v_strides, out, batch, tokens, heads, head_dim, block, scale,
+                    tau, sink_kv, sink_q, int8 != 0, int8_pv != 0, SOLB200_STAGES_ALL, workspace,
+                    workspace_bytes, nullptr, nullptr, stream, order);
+}
+
 int32_t solb200_debug_set_wait(int64_t wait_ns, int32_t stall_unit) {
   if (stall_unit < -1) return fail(SOLB200_ERR_INVALID, "stall_unit must be -1 (none) or a unit id");
   g_debug_wait.wait_ns = wait_ns > 0 ? (uint64_t)wait_ns : SOLB200_WAIT_NS;
@@ -402,6 +464,9 @@ int32_t solb200_read_device_error(void* workspace, int32_t* code, void* stream) 
   e = cudaMemsetAsync(workspace, 0, sizeof(int32_t), st);
   if (e != cudaSuccess) return cuda_fail(e, "clearing the device error word");
   *code = host;
+  if (host & kErrBadIndex)
+    return fail(SOLB200_ERR_INVALID, "the token order holds an index outside [0, tokens) (device error bits " +
+                                         std::to_string(host) + ")");
   if (host != 0)
     return fail(SOLB200_ERR_TIMEOUT, "a kernel gave up on a bounded wait (device error bits " +
                                          std::to_string(host) + ")");

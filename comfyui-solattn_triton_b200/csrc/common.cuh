@@ -25,7 +25,20 @@ enum DeviceError : int {
   kErrWaitSoftmax = 4,   // softmax warps waited too long for scores
   kErrWaitEpilogue = 8,  // epilogue waited too long for the last P*V
   kErrWaitDrain = 16,    // exit path could not drain in-flight copies / MMAs
+  kErrBadIndex = 32,     // a token-order index outside [0, tokens) (read as token 0, not stored)
 };
+
+// Token of row r under an optional token order: perm[r] when it lies in [0, T), else
+// token 0 with kErrBadIndex recorded (so no access leaves the tensor).
+__device__ __forceinline__ int64_t order_row(const int64_t* perm, int64_t r, int64_t T, int* err) {
+  if (!perm) return r;
+  const int64_t t = __ldg(perm + r);
+  if (t < 0 || t >= T) {
+    if (err) atomicOr(err, kErrBadIndex);
+    return 0;
+  }
+  return t;
+}
 
 // Programmatic dependent launch. Every kernel of the path is launched with
 // programmaticStreamSerializationAllowed (launch_pdl), and its first statement is

@@ -21,6 +21,10 @@ struct FwdParams {
   // a barrier that nothing completes, so that its pipeline waits run out
   uint64_t wait_ns;
   int stall_unit;
+  // reordered calls: row i of the attention sequence is output token perm[i]; the
+  // epilogue writes each row to out[b, perm[i], h, :] (dense BTHD) instead of the tile store
+  const int64_t* perm;
+  __nv_bfloat16* out;
 };
 
 struct FwdMaps {
@@ -51,6 +55,32 @@ __device__ __forceinline__ UnitInfo decode_unit(const FwdParams& p, int cta) {
 }
 
 enum { kTileApprox = 0, kTileExact = 1 };
+
+// Epilogue of a reordered call: the unit's output tile, staged bf16 in shared memory as
+// HD/64 boxes of BLK rows x 128 bytes (128-byte swizzle, box i at sO + i * BLK * 128), is
+// written row by row to out[b, perm[qb*BLK + r], h, :]; warp w of the `nwarps` epilogue warps
+// stores rows w, w + nwarps, ..., one coalesced row (HD * 2 bytes over the 32 lanes) per
+// store. Rows past T are not stored; an index outside [0, T) is recorded and skipped.
+template <int HD, int BLK>
+__device__ __forceinline__ void store_rows_reordered(const uint8_t* sO, const FwdParams& p, const UnitInfo& u,
+                                                     int warp, int nwarps, int lane) {
+  constexpr int LB = HD * 2 / 32;                 // bytes per lane: 8 (HD 128) or 4 (HD 64)
+  const int byte0 = lane * LB;                     // byte of the output row this lane stores
+  const int box = byte0 >> 7, cb = byte0 & 127;    // 64-column box, byte inside its 128-byte row
+  for (int r = warp; r < BLK; r += nwarps) {
+    const int64_t pos = (int64_t)u.qb * BLK + r;
+    if (pos >= p.T) break;
+    const int64_t tok = __ldg(p.perm + pos);
+    if (tok < 0 || tok >= p.T) {
+      if (lane == 0) atomicOr(p.err, kErrBadIndex);
+      continue;
+    }
+    const uint8_t* src = sO + box * (BLK * 128) + r * 128 + ((((cb >> 4) ^ (r & 7)) << 4) | (cb & 15));
+    uint8_t* dst = reinterpret_cast<uint8_t*>(p.out + (((int64_t)u.b * p.T + tok) * p.H + u.h) * HD) + byte0;
+    if (LB == 8) *reinterpret_cast<uint2*>(dst) = *reinterpret_cast<const uint2*>(src);
+    else *reinterpret_cast<uint32_t*>(dst) = *reinterpret_cast<const uint32_t*>(src);
+  }
+}
 
 __device__ __forceinline__ uint32_t low_bits(int n) {
   return n >= 32 ? 0xffffffffu : (n <= 0 ? 0u : ((1u << n) - 1u));

@@ -541,7 +541,9 @@ sol_fwd_int8_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_const
       fence_proxy_async_smem();
     }
     named_bar_sync(1, 128);
-    if (ok && j > 0 && threadIdx.x == 0) {
+    if (ok && j > 0 && p.perm) {
+      store_rows_reordered<HD, BLK>(sQ, p, u, warp, 4, lane);
+    } else if (ok && j > 0 && threadIdx.x == 0) {
       for (int i = 0; i < NBOX; ++i) tma_store_4d(&tm_o, sQ + i * (BLK * 128), i * 64, u.h, u.qb * BLK, u.b);
       bulk_commit_group();
       bulk_wait_group_read0();

@@ -108,15 +108,19 @@ __global__ void __launch_bounds__(64) pool_kernel(PoolParams p) {
   const int r1 = min(p.T, r0 + p.blk);
   const __nv_bfloat16* src;
   int64_t st;
+  __nv_bfloat16* copy;   // the reordered dense copy of this role's tensor, or null
   if (role == 0) {
     src = p.q + (int64_t)b * p.sq_b + (int64_t)h * p.sq_h + d0;
     st = p.sq_t;
+    copy = p.qcopy;
   } else if (role == 1) {
     src = p.k + (int64_t)b * p.sk_b + (int64_t)h * p.sk_h + d0;
     st = p.sk_t;
+    copy = p.kcopy;
   } else {
     src = p.v + (int64_t)b * p.sv_b + (int64_t)h * p.sv_h + d0;
     st = p.sv_t;
+    copy = p.vcopy;
   }
   float sum[8], vmax[8];
 #pragma unroll
@@ -126,12 +130,14 @@ __global__ void __launch_bounds__(64) pool_kernel(PoolParams p) {
 #pragma unroll
     for (int j = 0; j < ROWS; ++j)
       u[j] = (active && rb + j < r1)
-                 ? __ldg(reinterpret_cast<const uint4*>(src + (int64_t)(rb + j) * st))
+                 ? __ldg(reinterpret_cast<const uint4*>(src + order_row(p.perm, rb + j, p.T, p.err) * st))
                  : make_uint4(0, 0, 0, 0);
 #pragma unroll
     for (int j = 0; j < ROWS; ++j) {
       const int r = rb + j;
       if (r >= r1) break;   // uniform over the CTA
+      if (copy && active)
+        *reinterpret_cast<uint4*>(copy + (((int64_t)b * p.T + r) * p.H + h) * HD + d0) = u[j];
       float x[8];
       {
         const __nv_bfloat162* hx = reinterpret_cast<const __nv_bfloat162*>(&u[j]);
@@ -608,10 +614,11 @@ __global__ void __launch_bounds__(256, 3) quant_kv_kernel(QuantParams p) {
   for (int i = 0; i < TOK; ++i) {
     const bool ok = active && t0 + i < p.T;
     const int t = ok ? t0 + i : 0;
-    uk[i] = ok ? __ldg(reinterpret_cast<const uint4*>(p.k + (int64_t)b * p.sk_b + (int64_t)t * p.sk_t +
+    const int64_t src_t = ok ? order_row(p.perm, t, p.T, p.err) : 0;   // token of row t
+    uk[i] = ok ? __ldg(reinterpret_cast<const uint4*>(p.k + (int64_t)b * p.sk_b + src_t * p.sk_t +
                                                       (int64_t)h * p.sk_h + d0))
                : make_uint4(0, 0, 0, 0);
-    uv[i] = ok && with_v ? __ldg(reinterpret_cast<const uint4*>(p.v + (int64_t)b * p.sv_b + (int64_t)t * p.sv_t +
+    uv[i] = ok && with_v ? __ldg(reinterpret_cast<const uint4*>(p.v + (int64_t)b * p.sv_b + src_t * p.sv_t +
                                                                (int64_t)h * p.sv_h + d0))
                          : make_uint4(0, 0, 0, 0);
   }

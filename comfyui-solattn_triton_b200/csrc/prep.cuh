@@ -13,6 +13,11 @@ struct PoolParams {
   float* vamax;                               // [B, N, H, D] or null
   int8_t* qi;                                 // [B, T, H, D] or null
   float* qs;                                  // [B, H, tp] or null
+  // token order (reordered calls): row r of every tensor is input token perm[r]; the
+  // rows are also written, in that order, to the dense copies that are non-null
+  const int64_t* perm;                        // [T] or null
+  __nv_bfloat16* qcopy; __nv_bfloat16* kcopy; __nv_bfloat16* vcopy;   // [B, T, H, D] or null
+  int* err;                                   // device error word (perm index out of range)
   int B, T, H, N, npad, blk, tp;              // tp = N * blk (row stride of qs)
 };
 
@@ -48,6 +53,8 @@ struct QuantParams {
   const float* vscale;   // [B, H, D] or null
   int8_t* ki; float* ks; // [B, T, H, D], [B, H, tp]
   int8_t* vi;            // [B, T, H, D] or null
+  const int64_t* perm;   // [T] token order (reordered calls) or null
+  int* err;              // device error word (perm index out of range)
   int B, T, H, tp;       // tp = N * blk (row stride of ks)
 };
 

@@ -69,16 +69,25 @@ def _offset(geom, which) -> int:
     return n.value
 
 
-class Workspace:
-    """A workspace allocation plus typed views of its intermediates."""
+def workspace_bytes_reordered(B, T, H, D, block=BLOCK, int8=False, int8_pv=True) -> int:
+    n = c_int64(0)
+    check(lib().solb200_workspace_bytes_reordered(B, T, H, D, block, int(int8), int(bool(int8_pv)),
+                                                  ctypes.byref(n)), "workspace_bytes_reordered")
+    return n.value
 
-    def __init__(self, B, T, H, D, block, int8, device):
+
+class Workspace:
+    """A workspace allocation plus typed views of its intermediates (``reordered``: sized
+    for solb200_sol_attn_reordered, the same offsets plus the reordered copies)."""
+
+    def __init__(self, B, T, H, D, block, int8, device, reordered=False, int8_pv=True):
         self.geom = (B, T, H, D, block, int(int8))
         self.B, self.T, self.H, self.D, self.block = B, T, H, D, block
         self.N = -(-T // block)
         self.npad = -(-self.N // 64) * 64
         self.nw = -(-self.N // 32)
-        self.nbytes = workspace_bytes(B, T, H, D, block, int8)
+        self.nbytes = (workspace_bytes_reordered(B, T, H, D, block, int8, int8_pv) if reordered
+                       else workspace_bytes(B, T, H, D, block, int8))
         self.buf = torch.empty(self.nbytes, dtype=torch.uint8, device=device)
 
     def ptr(self) -> int:
@@ -97,6 +106,33 @@ class Workspace:
         stream = _stream_ptr(self.buf.device)
         check(lib().solb200_read_device_error(self.ptr(), ctypes.byref(code), stream),
               "device error check")
+
+
+def _attn_reordered(q, k, v, order, *, scale, tau, sink_blocks, sink_q, block, int8, int8_pv):
+    """solb200_sol_attn_reordered: the call on tokens taken in `order`, output in input order."""
+    q, k, v = _ready(q, "q"), _ready(k, "k"), _ready(v, "v")
+    if q.shape != k.shape or q.shape != v.shape:
+        raise RuntimeError(f"solb200: q/k/v shapes differ: {tuple(q.shape)}, {tuple(k.shape)}, "
+                           f"{tuple(v.shape)}")
+    B, T, H, D = q.shape
+    if not torch.is_tensor(order) or order.dtype != torch.int64 or order.dim() != 1 or order.numel() != T:
+        raise RuntimeError("solb200: token_order must be an int64 tensor of one index per token")
+    if order.device != q.device:
+        raise RuntimeError("solb200: token_order must be on the tensors' device")
+    order = order.contiguous()
+    scale = D ** -0.5 if scale is None else float(scale)
+    with torch.cuda.device(q.device):
+        ws = Workspace(B, T, H, D, block, int8, q.device, reordered=True, int8_pv=int8_pv)
+        out = torch.empty((B, T, H, D), dtype=torch.bfloat16, device=q.device)
+        rc = lib().solb200_sol_attn_reordered(
+            q.data_ptr(), _strides(q), k.data_ptr(), _strides(k), v.data_ptr(), _strides(v), out.data_ptr(),
+            B, T, H, D, block, scale, float(tau), I64x2(int(sink_blocks[0]), int(sink_blocks[1])),
+            I64x2(int(sink_q[0]), int(sink_q[1])), order.data_ptr(), int(bool(int8)), int(bool(int8_pv)),
+            ws.ptr(), ws.nbytes, _stream_ptr(q.device))
+        check(rc, "sol_attn (token order)")
+        if _SYNC_CHECK:
+            ws.check_device_error()
+    return out
 
 
 def _attn(q, k, v, *, scale, tau, sink_blocks, sink_q, block, int8, int8_pv, stages,
@@ -134,17 +170,26 @@ def _attn(q, k, v, *, scale, tau, sink_blocks, sink_q, block, int8, int8_pv, sta
 
 
 def sol_attn(q, k, v, *, scale=None, tau=1.0, sink_blocks=(0, 0), sink_q=(0, 0), use_tma=False,
-             block=BLOCK):
+             block=BLOCK, token_order=None):
     """BF16 Sol-Attn on BTHD inputs. ``use_tma`` is accepted for signature parity and
-    ignored: the sm_100a kernel always stages tiles with TMA."""
+    ignored: the sm_100a kernel always stages tiles with TMA. ``token_order`` (this build's
+    addition; int64 [T] on the device, e.g. a Morton permutation): attend over the tokens
+    in that order and return the output in input order, equal to
+    ``sol_attn(q[:, order], ...)[:, inverse]`` without the two gather passes."""
+    if token_order is not None:
+        return _attn_reordered(q, k, v, token_order, scale=scale, tau=tau, sink_blocks=sink_blocks,
+                               sink_q=sink_q, block=block, int8=False, int8_pv=False)
     out, _, _, _ = _attn(q, k, v, scale=scale, tau=tau, sink_blocks=sink_blocks, sink_q=sink_q,
                          block=block, int8=False, int8_pv=False, stages=STAGES_ALL)
     return out
 
 
 def sol_attn_int8(q, k, v, *, scale=None, tau=1.0, sink_blocks=(0, 0), sink_q=(0, 0),
-                  use_tma=False, int8_pv=True, block=BLOCK):
+                  use_tma=False, int8_pv=True, block=BLOCK, token_order=None):
     """Sol-Attn with an INT8 exact branch. Same contract as ``sol_attn``."""
+    if token_order is not None:
+        return _attn_reordered(q, k, v, token_order, scale=scale, tau=tau, sink_blocks=sink_blocks,
+                               sink_q=sink_q, block=block, int8=True, int8_pv=int8_pv)
     out, _, _, _ = _attn(q, k, v, scale=scale, tau=tau, sink_blocks=sink_blocks, sink_q=sink_q,
                          block=block, int8=True, int8_pv=int8_pv, stages=STAGES_ALL)
     return out

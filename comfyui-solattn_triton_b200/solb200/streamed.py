@@ -10,7 +10,9 @@ into chunks and the three costs of a host-resident call overlap instead of addin
 Host -> device and device -> host run on separate copy engines, so a call costs about
 the host -> device transfer of q, k and v plus one chunk's compute and copy-out. Each
 head's output is bit-identical to ``sol_attn`` / ``sol_attn_int8`` on device tensors.
-Device memory: two chunk slots of q, k, v, out plus one workspace, for the call.
+Device memory: two chunk slots of q, k, v, out plus one workspace. They and the two copy
+streams are kept per (device, geometry) across calls (``release_host_buffers`` frees
+them), so a repeated call allocates nothing and creates no stream.
 
 The reference has no host-memory entry point (its wrappers receive device tensors);
 this is this build's addition for callers that keep activations in host memory.
@@ -27,15 +29,40 @@ H2D, D2H = 1, 0
 
 
 def plan_chunks(heads: int, heads_per_chunk: int | None = None) -> list[tuple[int, int]]:
-    """(first head, head count) of each chunk. Default: max(2, heads // 16) heads, which
-    measured best at config 3 (2-head chunks: 19.7 ms per host-to-host call against
-    20.3 ms for 5-head and 22.3 ms for 10-head chunks)."""
+    """(first head, head count) of each chunk. Default: 2 heads from 16 heads up (at 40
+    heads 2-head chunks measured 19.7 ms per host-to-host call against 20.3 ms for 5-head
+    and 22.3 ms for 10-head chunks), single heads below, so that a rank with few heads
+    still has at least four chunks in flight and only the first copy-in and the last
+    copy-out are exposed."""
     if heads < 1:
         raise ValueError("heads must be positive")
-    hc = heads_per_chunk if heads_per_chunk else min(heads, max(2, heads // 16))
+    hc = heads_per_chunk if heads_per_chunk else min(heads, 2 if heads >= 16 else 1)
     if hc < 1:
         raise ValueError("heads_per_chunk must be positive")
     return [(h0, min(hc, heads - h0)) for h0 in range(0, heads, hc)]
+
+
+_BUFFERS = {}
+
+
+def _buffers(dev, B, T, hc, D, block, int8):
+    """Copy streams, two chunk slots of q, k, v, out and a workspace for this geometry,
+    created on first use and kept for later calls."""
+    key = (str(dev), B, T, hc, D, block, bool(int8))
+    hit = _BUFFERS.get(key)
+    if hit is None:
+        hit = dict(s_in=torch.cuda.Stream(dev), s_out=torch.cuda.Stream(dev),
+                   slots=[[torch.empty((B, T, hc, D), dtype=torch.bfloat16, device=dev) for _ in range(4)]
+                          for _ in range(2)],
+                   ws=Workspace(B, T, hc, D, block, int8, dev))
+        _BUFFERS[key] = hit
+    return hit
+
+
+def release_host_buffers():
+    """Free the device buffers and streams kept by sol_attn_host (after a synchronize)."""
+    torch.cuda.synchronize()
+    _BUFFERS.clear()
 
 
 def _check_host(t: torch.Tensor, name: str):
@@ -72,13 +99,12 @@ def sol_attn_host(q, k, v, *, scale=None, tau=1.0, sink_blocks=(0, 0), sink_q=(0
     L = lib()
     with torch.cuda.device(dev):
         comp = torch.cuda.current_stream(dev)
-        s_in, s_out = torch.cuda.Stream(dev), torch.cuda.Stream(dev)
-        # the copy streams start after whatever the caller queued on its stream
+        bufs = _buffers(dev, B, T, hc, D, block, int8)
+        s_in, s_out, slots, ws = bufs["s_in"], bufs["s_out"], bufs["slots"], bufs["ws"]
+        # the copy streams start after whatever the caller queued on its stream (which
+        # includes the previous call's last copy-out, so the kept slots are free again)
         s_in.wait_stream(comp)
         s_out.wait_stream(comp)
-        slots = [[torch.empty((B, T, hc, D), dtype=torch.bfloat16, device=dev) for _ in range(4)]
-                 for _ in range(2)]
-        ws = Workspace(B, T, hc, D, block, int8, dev)
         sk, sq = I64x2(int(sink_blocks[0]), int(sink_blocks[1])), I64x2(int(sink_q[0]), int(sink_q[1]))
         ev_in, ev_comp, ev_out = [], [], []
         for i, (h0, n) in enumerate(chunks):
@@ -114,11 +140,8 @@ def sol_attn_host(q, k, v, *, scale=None, tau=1.0, sink_blocks=(0, 0), sink_q=(0
             ev_in.append(e_in)
             ev_comp.append(e_comp)
             ev_out.append(e_out)
+        # the caller's stream (and so the next call) waits for the last copy-out
         comp.wait_event(ev_out[-1])
-        # keep the chunk buffers alive until the streams are done with them
-        for buf in [t for slot in slots for t in slot] + [ws.buf]:
-            buf.record_stream(s_in)
-            buf.record_stream(s_out)
         if synchronize:
             ev_out[-1].synchronize()
     return out

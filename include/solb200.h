@@ -23,6 +23,8 @@
  *                                             roll of _perm_for, _morton_h3.py:42-61
  *   solb200_gather_rows     x.index_select(1, perm) of the Morton hooks,
  *                                             _morton.py:128,148, _morton_h3.py:192-217
+ *   solb200_sol_attn_reordered  the Morton hooks' gathers (_morton.py:115-148,
+ *                                             _morton_h3.py:161-218) fused around one call
  */
 #ifndef SOLB200_H
 #define SOLB200_H
@@ -119,6 +121,36 @@ SOLB200_API int32_t solb200_sol_attn_int8(const void* q, const int64_t* q_stride
                               const int64_t* sink_kv, const int64_t* sink_q, int32_t int8_pv,
                               int32_t stages, void* workspace, int64_t workspace_bytes,
                               int32_t* lists, float* route_stat, void* stream);
+
+/* Bytes of workspace for solb200_sol_attn_reordered with this geometry: the workspace of
+ * solb200_workspace_bytes (same offsets) plus dense copies of q / k / v in the call's token
+ * order for the tensors the forward reads by tiles (q; k for BF16; v for BF16 or without
+ * int8 P*V). */
+SOLB200_API int32_t solb200_workspace_bytes_reordered(int64_t batch, int64_t tokens, int64_t heads,
+                                                      int64_t head_dim, int32_t block, int32_t int8,
+                                                      int32_t int8_pv, int64_t* bytes);
+
+/* Sol-Attn with the tokens taken in the order `order` (int64 device array of `tokens`
+ * entries, a permutation of [0, tokens); position i of the attention sequence is input
+ * token order[i]) and the output written back in input order: the same result, bit for bit,
+ * as gathering q/k/v by order, calling solb200_sol_attn_bf16 (int8 = 0) or
+ * solb200_sol_attn_int8 (int8 = 1, int8_pv as there) and gathering the output by the
+ * inverse order. That is the Morton reordering of the reference's model hooks
+ * (_morton.py:115-148, _morton_h3.py:161-218: x.index_select(1, perm) before the blocks,
+ * index_select(1, inverse) after) applied around one call, without the gather passes: the
+ * pooling pass reads q/k/v rows through `order` (writing the copies the forward's tile
+ * loads need) and the forward writes each output row to its input position. An index
+ * outside [0, tokens) is recorded in the device error word (solb200_read_device_error then
+ * returns SOLB200_ERR_INVALID) and never dereferenced; repeated indices are the caller's
+ * error. Workspace: solb200_workspace_bytes_reordered. */
+SOLB200_API int32_t solb200_sol_attn_reordered(const void* q, const int64_t* q_strides, const void* k,
+                                               const int64_t* k_strides, const void* v,
+                                               const int64_t* v_strides, void* out, int64_t batch,
+                                               int64_t tokens, int64_t heads, int64_t head_dim,
+                                               int32_t block, float scale, float tau,
+                                               const int64_t* sink_kv, const int64_t* sink_q,
+                                               const int64_t* order, int32_t int8, int32_t int8_pv,
+                                               void* workspace, int64_t workspace_bytes, void* stream);
 
 /* BF16 Sol-Attn that allocates nothing, for hosts that cannot hand this library device
  * memory at call time (an application that plans all device allocations up front and

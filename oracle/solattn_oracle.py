@@ -552,3 +552,41 @@ def dense_reference(q, k, v, scale=None):
                   for x in (q, k, v))
     o = torch.nn.functional.scaled_dot_product_attention(qt, kt, vt, scale=scale)
     return o.permute(0, 2, 1, 3).contiguous().numpy()
+
+
+# ------------------------------------------------------------- CPU timing arm
+
+def unit_runner(q, k, v, *, tau, block, path="bf16", int8_pv=True, scale=None, group=64):
+    """For timing the reference's algorithm on host cores (bench.py's CPU legs): run the
+    call's preprocess once (``prepare`` / ``fused_preprocess``, the same code as
+    ``sol_attn`` / ``sol_attn_int8``) and return ``run(units)``, which computes the output
+    tiles of the given (b, h, q_block) units exactly as those functions do (a list of
+    [block, D] float32 tiles, rows past T included)."""
+    B, T, H, D = q.shape
+    scale = D ** -0.5 if scale is None else float(scale)
+    N = -(-T // block)
+    s2 = _log2_scale(scale)
+    no_sink = (0, 0)
+    if path == "int8":
+        parts = fused_preprocess(q, k, v, tau, scale, T, block, int8_pv)
+        kcp, vcp = _pad_rows(parts["kc"], group), _pad_rows(parts["vc"], group)
+
+        def run(units):
+            tiles = []
+            for b, h, n in units:
+                r0 = n * block
+                tiles.append(_fwd_unit_int8(_tile(q[b, :, h], r0, block), _tile(parts["qi"][b, :, h], r0, block),
+                               _tile(parts["qs"][b, :, h], r0, block), parts["ki"][b, :, h],
+                               parts["ks"][b, :, h], parts["vi"][b, :, h] if int8_pv else None, v[b, :, h],
+                               parts["vsc"][b, h] if int8_pv else None, kcp[b, :, h], vcp[b, :, h],
+                               parts["thr"][b, n, h], n, T, N, block, s2, no_sink, no_sink, group, int8_pv))
+            return tiles
+    else:
+        kc, vc, thr = prepare(q, k, v, tau, scale, T, block)
+        kcp, vcp = _pad_rows(kc, group), _pad_rows(vc, group)
+
+        def run(units):
+            return [_fwd_unit_bf16(_tile(q[b, :, h], n * block, block), k[b, :, h], v[b, :, h], kcp[b, :, h],
+                                   vcp[b, :, h], thr[b, n, h], n, T, N, block, s2, no_sink, no_sink, group)
+                    for b, h, n in units]
+    return run

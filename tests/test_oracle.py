@@ -128,3 +128,17 @@ def test_routing_mask_restatement_consistent():
             if 0 <= j < N:
                 assert mask[:, :, n, j].all()
     assert 0 < mask.mean() < 1
+
+
+@pytest.mark.parametrize("path", ["bf16", "int8"])
+def test_unit_runner_matches_full_call(path):
+    """The CPU timing arm's unit runner computes the same tiles as the full oracle call."""
+    g = load_golden("c1")
+    B, T, H, D, blk = golden_meta(g)
+    run = O.unit_runner(g["q"], g["k"], g["v"], tau=0.9, block=blk, path=path)
+    units = [(0, 1, 2), (0, 0, T // blk - 1)]
+    fn = O.sol_attn_int8 if path == "int8" else O.sol_attn
+    full = fn(g["q"], g["k"], g["v"], tau=0.9, block=blk, units=units)
+    for (b, h, n), tile in zip(units, run(units)):
+        r1 = min(T, (n + 1) * blk)
+        assert np.array_equal(tile[: r1 - n * blk], full[b, n * blk:r1, h])

@@ -11,9 +11,10 @@ from solb200.streamed import plan_chunks
 
 def test_plan_chunks():
     assert plan_chunks(40) == [(h, 2) for h in range(0, 40, 2)]
-    assert plan_chunks(64) == [(h, 4) for h in range(0, 64, 4)]
+    assert plan_chunks(64) == [(h, 2) for h in range(0, 64, 2)]
+    assert plan_chunks(5) == [(h, 1) for h in range(5)]     # a rank of eight at 40 heads
     assert plan_chunks(6, 4) == [(0, 4), (4, 2)]
-    assert plan_chunks(3) == [(0, 2), (2, 1)]
+    assert plan_chunks(3) == [(0, 1), (1, 1), (2, 1)]
     assert plan_chunks(1) == [(0, 1)]
     assert plan_chunks(1, 8) == [(0, 1)]
     with pytest.raises(ValueError):
@@ -40,3 +41,19 @@ def test_streamed_equals_device_call(cuda_device, shape, block, hpc, int8):
     want = fn(q.cuda(), k.cuda(), v.cuda(), tau=0.9, block=block).cpu()
     assert got.shape == want.shape and got.dtype == torch.bfloat16
     assert torch.equal(got, want)
+
+
+@pytest.mark.gpu
+def test_streamed_buffers_kept_across_calls(cuda_device):
+    """Back-to-back calls (no synchronisation in between) reuse the kept chunk slots and
+    streams; each call's output is its own device call's."""
+    g = torch.Generator().manual_seed(4)
+    shape = (1, 4096, 5, 128)
+    inputs = [tuple(torch.randn(*shape, generator=g).to(torch.bfloat16).pin_memory() for _ in range(3))
+              for _ in range(3)]
+    outs = [solb200.sol_attn_host(*x, tau=0.9, block=128, synchronize=False) for x in inputs]
+    torch.cuda.synchronize()
+    for x, got in zip(inputs, outs):
+        want = solb200.sol_attn(*(t.cuda() for t in x), tau=0.9, block=128).cpu()
+        assert torch.equal(got, want)
+    solb200.release_host_buffers()
