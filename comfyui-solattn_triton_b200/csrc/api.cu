@@ -298,6 +298,7 @@ int32_t run(const Plan& P, const Call& c) {
   fp.order = at<int>(c.ws, P, SOLB200_BUF_ORDER);
   fp.err = err;
   fp.B = (int)P.B; fp.T = (int)P.T; fp.H = (int)P.H; fp.N = P.N; fp.nw = P.nw;
+  fp.Tk = (int)P.T; fp.Nk = P.N;
   fp.s2 = s2;
   fp.wait_ns = g_debug_wait.wait_ns;
   fp.stall_unit = g_debug_wait.stall_unit;
@@ -445,6 +446,59 @@ int32_t solb200_sol_attn_reordered(const void* q, const int64_t* q_strides, cons
   return attn_entry(q, q_strides, k, k_strides, v, v_strides, out, batch, tokens, heads, head_dim, block, scale,
                     tau, sink_kv, sink_q, int8 != 0, int8_pv != 0, SOLB200_STAGES_ALL, workspace,
                     workspace_bytes, nullptr, nullptr, stream, order);
+}
+
+int32_t solb200_attn_dense(const void* q, const int64_t* q_strides, const void* k, const int64_t* k_strides,
+                           const void* v, const int64_t* v_strides, void* out, int64_t batch, int64_t q_tokens,
+                           int64_t kv_tokens, int64_t heads, int64_t head_dim, float scale, void* workspace,
+                           int64_t workspace_bytes, void* stream) {
+  int32_t rc = check_device();
+  if (rc) return rc;
+  if (batch < 1 || q_tokens < 1 || kv_tokens < 1 || heads < 1)
+    return fail(SOLB200_ERR_INVALID, "batch, tokens and heads must be >= 1");
+  if (head_dim != 64 && head_dim != 128) return fail(SOLB200_ERR_INVALID, "head_dim must be 64 or 128");
+  if (q_tokens > ((int64_t)1 << 30) || kv_tokens > ((int64_t)1 << 30))
+    return fail(SOLB200_ERR_INVALID, "tokens must be < 2^30");
+  constexpr int BLK = 128;
+  const int64_t nq = (q_tokens + BLK - 1) / BLK, nk = (kv_tokens + BLK - 1) / BLK;
+  if (batch * heads * nq >= ((int64_t)1 << 31)) return fail(SOLB200_ERR_INVALID, "too many query blocks");
+  if ((rc = check_tensor("q", q, q_strides, batch))) return rc;
+  if ((rc = check_tensor("k", k, k_strides, batch))) return rc;
+  if ((rc = check_tensor("v", v, v_strides, batch))) return rc;
+  if (!out || !aligned16(out)) return fail(SOLB200_ERR_ALIGNMENT, "out: null or not 16-byte aligned");
+  if (!workspace || workspace_bytes < 256)
+    return fail(SOLB200_ERR_WORKSPACE, "the dense call needs a workspace of at least 256 bytes");
+  if (!aligned16(workspace)) return fail(SOLB200_ERR_ALIGNMENT, "workspace not 16-byte aligned");
+  if (!(scale > 0.f)) return fail(SOLB200_ERR_INVALID, "scale must be > 0");
+  const cudaStream_t st = static_cast<cudaStream_t>(stream);
+  int* err = static_cast<int*>(workspace);
+  cudaError_t e = cudaMemsetAsync(err, 0, sizeof(int), st);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaMemsetAsync(error word)");
+  FwdParams fp{};
+  fp.mask = nullptr;   // dense: every key block exact
+  fp.order = nullptr;
+  fp.err = err;
+  fp.B = (int)batch; fp.T = (int)q_tokens; fp.H = (int)heads; fp.N = (int)nq; fp.nw = (int)((nk + 31) / 32);
+  fp.Tk = (int)kv_tokens; fp.Nk = (int)nk;
+  fp.s2 = scale * 1.4426950408889634f;
+  fp.wait_ns = g_debug_wait.wait_ns;
+  fp.stall_unit = g_debug_wait.stall_unit;
+  fp.perm = nullptr;
+  fp.out = static_cast<__nv_bfloat16*>(out);
+  FwdMaps m;
+  const int64_t D = head_dim, H = heads;
+  if ((rc = make_map(&m.q, q, false, D, H, q_tokens, batch, q_strides[2], q_strides[1], q_strides[0], 128, "q")))
+    return rc;
+  if ((rc = make_map(&m.k, k, false, D, H, kv_tokens, batch, k_strides[2], k_strides[1], k_strides[0], 64, "k")))
+    return rc;
+  if ((rc = make_map(&m.v, v, false, D, H, kv_tokens, batch, v_strides[2], v_strides[1], v_strides[0], 64, "v")))
+    return rc;
+  if ((rc = make_map(&m.o, out, false, D, H, q_tokens, batch, D, H * D, q_tokens * H * D, BLK, "out"))) return rc;
+  m.kc = m.k;   // no pooled keys / values in a dense call: valid maps that are never loaded
+  m.vc = m.v;
+  e = launch_fwd_bf16((int)head_dim, BLK, m, fp, st);
+  if (e != cudaSuccess) return cuda_fail(e, "dense forward launch");
+  return SOLB200_OK;
 }
 
 int32_t solb200_debug_set_wait(int64_t wait_ns, int32_t stall_unit) {

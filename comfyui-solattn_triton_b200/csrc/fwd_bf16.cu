@@ -57,6 +57,7 @@ sol_fwd_bf16_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_const
   uint64_t* bar_drain = bars + 11;
   uint64_t* bar_never = bars + 12;       // completed by nothing (the stall_unit test hook)
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 13);
+  int64_t* sTok = reinterpret_cast<int64_t*>(bars + 32);   // [128] output tokens (reordered calls)
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const UnitInfo u = decode_unit(p, blockIdx.x);
@@ -185,6 +186,7 @@ sol_fwd_bf16_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_const
     // ------------------------------------------------- softmax + epilogue (rows)
     const int row = threadIdx.x;                       // 0..127 = TMEM lane
     const uint32_t lane_base = (uint32_t)(warp * 32) << 16;
+    if (p.perm) prefetch_row_token<BLK>(p, u, row, sTok);
     float m_ref = -INFINITY, l_sum = 0.f;
     HalfIter<BLK> it(p, u);
     int s = 0, kind, row0;
@@ -205,9 +207,9 @@ sol_fwd_bf16_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_const
         const int tail_col = (p.N - 1 >= row0 && p.N - 1 < row0 + 64) ? p.N - 1 - row0 : -1;
         softmax_half<true, true, HD>(ts, tO + lane_base, colmask, p.s2, m_ref, l_sum, s > 0, tail_col,
                                      (float)(p.T - (p.N - 1) * BLK), (float)BLK, drain);
-      } else if (row0 + 64 > p.T) {
-        colmask[0] = low_bits(p.T - row0);
-        colmask[1] = low_bits(p.T - row0 - 32);
+      } else if (row0 + 64 > p.Tk) {
+        colmask[0] = low_bits(p.Tk - row0);
+        colmask[1] = low_bits(p.Tk - row0 - 32);
         softmax_half<true, false, HD>(ts, tO + lane_base, colmask, p.s2, m_ref, l_sum, s > 0, -1, 0.f, 1.f,
                                       drain);
       } else {
@@ -248,7 +250,7 @@ sol_fwd_bf16_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_const
     }
     named_bar_sync(1, 128);
     if (ok && s > 0 && p.perm) {
-      store_rows_reordered<HD, BLK>(sQ, p, u, warp, 4, lane);
+      store_rows_reordered<HD, BLK>(sQ, sTok, p, u, warp, 4, lane);
     } else if (ok && s > 0 && threadIdx.x == 0) {
       for (int i = 0; i < NBOX; ++i) tma_store_4d(&tm_o, sQ + i * (BLK * 128), i * 64, u.h, u.qb * BLK, u.b);
       bulk_commit_group();
@@ -263,7 +265,8 @@ sol_fwd_bf16_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_const
   }
 }
 
-size_t fwd_bf16_smem_bytes(int hd) { return (size_t)(hd / 64) * (128 * 128 + 4 * 64 * 128) + 1024 + 256; }
+// q + K and V slots, barriers (256 B) and the output-token row (1 KB), plus 1 KB to align
+size_t fwd_bf16_smem_bytes(int hd) { return (size_t)(hd / 64) * (128 * 128 + 4 * 64 * 128) + 1024 + 256 + 1024; }
 
 template <int HD, int BLK>
 static cudaError_t launch_t(const FwdMaps& m, const FwdParams& p, cudaStream_t st) {

@@ -6,10 +6,12 @@
 namespace solb200 {
 
 struct FwdParams {
-  const uint32_t* mask;   // [B, H, N, nw] exact-block bits (routing output)
+  const uint32_t* mask;   // [B, H, N, nw] exact-block bits (routing output); null: dense
+                          // attention (every key block exact, no approximate tiles)
   const int* order;       // [B*H*N] unit of each CTA (the schedule), or null: CTA i = unit i
   int* err;               // device error word
-  int B, T, H, N, nw;
+  int B, T, H, N, nw;     // T, N: query tokens and query blocks (units per head)
+  int Tk, Nk;             // key tokens and key blocks (T and N except for dense cross-attention)
   float s2;               // softmax scale * log2(e)
   // INT8 path only
   const float* qs;        // [B, H, T] per-token Q scales
@@ -50,31 +52,45 @@ __device__ __forceinline__ UnitInfo decode_unit(const FwdParams& p, int cta) {
   const int bh = unit / p.N;
   u.b = bh / p.H;
   u.h = bh % p.H;
-  u.row = p.mask + ((int64_t)bh * p.N + u.qb) * p.nw;
+  u.row = p.mask ? p.mask + ((int64_t)bh * p.N + u.qb) * p.nw : nullptr;
   return u;
 }
 
 enum { kTileApprox = 0, kTileExact = 1 };
 
+// Reordered calls: the output token of this thread's tile row (row = query row of the
+// unit), prefetched at the start of the unit into sTok[row] so that the epilogue's stores
+// do not wait on it: perm[qb*BLK + row], or -1 for rows past T (not stored) and for an index
+// outside [0, T) (recorded in the error word, not stored).
+template <int BLK>
+__device__ __forceinline__ void prefetch_row_token(const FwdParams& p, const UnitInfo& u, int row, int64_t* sTok) {
+  if (row >= BLK) return;
+  const int64_t pos = (int64_t)u.qb * BLK + row;
+  int64_t tok = -1;
+  if (pos < p.T) {
+    tok = __ldg(p.perm + pos);
+    if (tok < 0 || tok >= p.T) {
+      atomicOr(p.err, kErrBadIndex);
+      tok = -1;
+    }
+  }
+  sTok[row] = tok;
+}
+
 // Epilogue of a reordered call: the unit's output tile, staged bf16 in shared memory as
 // HD/64 boxes of BLK rows x 128 bytes (128-byte swizzle, box i at sO + i * BLK * 128), is
-// written row by row to out[b, perm[qb*BLK + r], h, :]; warp w of the `nwarps` epilogue warps
-// stores rows w, w + nwarps, ..., one coalesced row (HD * 2 bytes over the 32 lanes) per
-// store. Rows past T are not stored; an index outside [0, T) is recorded and skipped.
+// written row by row to out[b, sTok[r], h, :] (the tokens prefetched by prefetch_row_token);
+// warp w of the `nwarps` epilogue warps stores rows w, w + nwarps, ..., one coalesced row
+// (HD * 2 bytes over the 32 lanes) per store; rows with token -1 are skipped.
 template <int HD, int BLK>
-__device__ __forceinline__ void store_rows_reordered(const uint8_t* sO, const FwdParams& p, const UnitInfo& u,
-                                                     int warp, int nwarps, int lane) {
+__device__ __forceinline__ void store_rows_reordered(const uint8_t* sO, const int64_t* sTok, const FwdParams& p,
+                                                     const UnitInfo& u, int warp, int nwarps, int lane) {
   constexpr int LB = HD * 2 / 32;                 // bytes per lane: 8 (HD 128) or 4 (HD 64)
   const int byte0 = lane * LB;                     // byte of the output row this lane stores
   const int box = byte0 >> 7, cb = byte0 & 127;    // 64-column box, byte inside its 128-byte row
   for (int r = warp; r < BLK; r += nwarps) {
-    const int64_t pos = (int64_t)u.qb * BLK + r;
-    if (pos >= p.T) break;
-    const int64_t tok = __ldg(p.perm + pos);
-    if (tok < 0 || tok >= p.T) {
-      if (lane == 0) atomicOr(p.err, kErrBadIndex);
-      continue;
-    }
+    const int64_t tok = sTok[r];
+    if (tok < 0) continue;
     const uint8_t* src = sO + box * (BLK * 128) + r * 128 + ((((cb >> 4) ^ (r & 7)) << 4) | (cb & 15));
     uint8_t* dst = reinterpret_cast<uint8_t*>(p.out + (((int64_t)u.b * p.T + tok) * p.H + u.h) * HD) + byte0;
     if (LB == 8) *reinterpret_cast<uint2*>(dst) = *reinterpret_cast<const uint2*>(src);
@@ -90,13 +106,14 @@ __device__ __forceinline__ uint32_t low_bits(int n) {
 // 128-block chunk of the pooled keys that holds at least one approximate (valid,
 // non-routed) block, then every routed block in ascending order.
 struct TileIter {
-  const uint32_t* row;
+  const uint32_t* row;    // null: dense (every one of the Nk key blocks is exact)
   int nw, N, nchunks;
   int phase, c, w;
   uint32_t bits;
 
   __device__ TileIter(const FwdParams& p, const UnitInfo& u)
-      : row(u.row), nw(p.nw), N(p.N), nchunks((p.N + 127) / 128), phase(0), c(0), w(-1), bits(0) {}
+      : row(u.row), nw(u.row ? p.nw : (p.Nk + 31) / 32), N(u.row ? p.N : p.Nk), nchunks((p.N + 127) / 128),
+        phase(u.row ? 0 : 1), c(0), w(-1), bits(0) {}
 
   // Approximate-column bits of pooled chunk `chunk` (128 columns = 4 words).
   __device__ __forceinline__ void approx_bits(int chunk, uint32_t (&out)[4]) const {
@@ -131,7 +148,7 @@ struct TileIter {
         return true;
       }
       if (++w >= nw) return false;
-      bits = row[w];
+      bits = row ? row[w] : low_bits(N - w * 32);
     }
   }
 };
@@ -148,7 +165,7 @@ struct HalfIter {
   int npend, ipend, pkind;
 
   __device__ HalfIter(const FwdParams& p, const UnitInfo& u)
-      : tiles(p, u), T(p.T), pend0(0), pend1(0), npend(0), ipend(0), pkind(0) {}
+      : tiles(p, u), T(p.Tk), pend0(0), pend1(0), npend(0), ipend(0), pkind(0) {}
 
   __device__ __forceinline__ bool next(int& kind, int& row0) {
     while (ipend >= npend) {

@@ -249,6 +249,7 @@ sol_fwd_int8_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_const
   uint64_t* bar_drain = bars + 14;
   uint64_t* bar_never = bars + 15;       // completed by nothing (the stall_unit test hook)
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 16);
+  int64_t* sTok = reinterpret_cast<int64_t*>(bars + 32);   // [128] output tokens (reordered calls)
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const UnitInfo u = decode_unit(p, blockIdx.x);
@@ -425,6 +426,7 @@ sol_fwd_int8_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_const
     // ------------------------------------------- softmax, fold and epilogue (rows)
     const int row = threadIdx.x;
     const uint32_t lane_base = (uint32_t)(warp * 32) << 16;
+    if (p.perm) prefetch_row_token<BLK>(p, u, row, sTok);
     const int qrow = u.qb * BLK + row;
     const float qs_log2 = (qrow < p.T ? __ldg(p.qs + (int64_t)bh * tp + qrow) : 0.f) * p.s2;
     float m_ref = -INFINITY, l_sum = 0.f;
@@ -458,7 +460,7 @@ sol_fwd_int8_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_const
 #pragma unroll
       for (int c = 0; c < BLK / 32; ++c) tmem_ld32(ts + c * 32, *reinterpret_cast<uint32_t(*)[32]>(&r[c * 32]));
       tmem_wait_ld();
-      const int valid = p.T - idx * BLK;
+      const int valid = p.Tk - idx * BLK;
       const float* ks = sKS + (e & 3) * BLK;
       if (valid < BLK) exact_scores<BLK, true>(r, ks, valid);
       else exact_scores<BLK, false>(r, ks, valid);
@@ -542,7 +544,7 @@ sol_fwd_int8_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_const
     }
     named_bar_sync(1, 128);
     if (ok && j > 0 && p.perm) {
-      store_rows_reordered<HD, BLK>(sQ, p, u, warp, 4, lane);
+      store_rows_reordered<HD, BLK>(sQ, sTok, p, u, warp, 4, lane);
     } else if (ok && j > 0 && threadIdx.x == 0) {
       for (int i = 0; i < NBOX; ++i) tma_store_4d(&tm_o, sQ + i * (BLK * 128), i * 64, u.h, u.qb * BLK, u.b);
       bulk_commit_group();
@@ -557,8 +559,9 @@ sol_fwd_int8_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_const
   }
 }
 
-// regions Q, K, V + key-scale ring + vscale + barriers, plus 1 KB to align the tiles
-static size_t fwd_int8_smem_bytes(int blk) { return (size_t)3 * 32768 + 4 * blk * 4 + 128 * 4 + 256 + 1024; }
+// regions Q, K, V + key-scale ring + vscale + barriers + the output-token row (1 KB), plus
+// 1 KB to align the tiles
+static size_t fwd_int8_smem_bytes(int blk) { return (size_t)3 * 32768 + 4 * blk * 4 + 128 * 4 + 256 + 1024 + 1024; }
 
 template <int HD, int BLK>
 static cudaError_t launch_t(const FwdMaps& m, const FwdParams& p, cudaStream_t st) {

@@ -106,6 +106,13 @@ __global__ void __launch_bounds__(64) pool_kernel(PoolParams p) {
   }
   const int r0 = n * p.blk;
   const int r1 = min(p.T, r0 + p.blk);
+  // reordered calls: the block's tokens, read once per CTA (checked) so that the row loads
+  // below do not wait behind an index load each
+  __shared__ int64_t s_tok[128];
+  if (p.perm) {
+    for (int i = threadIdx.x; i < r1 - r0; i += blockDim.x) s_tok[i] = order_row(p.perm, r0 + i, p.T, p.err);
+    __syncthreads();
+  }
   const __nv_bfloat16* src;
   int64_t st;
   __nv_bfloat16* copy;   // the reordered dense copy of this role's tensor, or null
@@ -130,7 +137,7 @@ __global__ void __launch_bounds__(64) pool_kernel(PoolParams p) {
 #pragma unroll
     for (int j = 0; j < ROWS; ++j)
       u[j] = (active && rb + j < r1)
-                 ? __ldg(reinterpret_cast<const uint4*>(src + order_row(p.perm, rb + j, p.T, p.err) * st))
+                 ? __ldg(reinterpret_cast<const uint4*>(src + (p.perm ? s_tok[rb + j - r0] : (int64_t)(rb + j)) * st))
                  : make_uint4(0, 0, 0, 0);
 #pragma unroll
     for (int j = 0; j < ROWS; ++j) {

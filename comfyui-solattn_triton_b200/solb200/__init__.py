@@ -7,9 +7,9 @@ backed by hand-written sm_100a kernels in ``libsolb200.so`` (C ABI in
 """
 
 from .morton import morton_perm, perm_for_span, permute_tokens, permute_tokens_many
-from .ops import BLOCK, fused_preprocess, prepare, routing, sol_attn, sol_attn_int8, workspace_bytes
+from .ops import BLOCK, dense_attn, fused_preprocess, prepare, routing, sol_attn, sol_attn_int8, workspace_bytes
 from .streamed import release_host_buffers, sol_attn_host
 
-__all__ = ["sol_attn", "sol_attn_int8", "prepare", "fused_preprocess", "routing", "morton_perm",
+__all__ = ["sol_attn", "sol_attn_int8", "dense_attn", "prepare", "fused_preprocess", "routing", "morton_perm",
            "perm_for_span", "permute_tokens", "permute_tokens_many", "workspace_bytes", "BLOCK",
            "sol_attn_host", "release_host_buffers"]

@@ -195,6 +195,35 @@ def sol_attn_int8(q, k, v, *, scale=None, tau=1.0, sink_blocks=(0, 0), sink_q=(0
     return out
 
 
+def dense_attn(q, k, v, *, scale=None):
+    """Dense BF16 attention softmax(q k^T * scale) v on the sm_100a tensor cores (C ABI
+    ``solb200_attn_dense``): q [B, Tq, H, D], k / v [B, Tk, H, D] (BTHD, any strides with a
+    contiguous head dim; Tq may differ from Tk), D 64 or 128; returns a fresh [B, Tq, H, D]
+    bf16 tensor. For the calls the Sol-Attn path declines (cross-attention, head_dim != 128,
+    short sequences), which the reference hands back to the host's attention."""
+    q, k, v = _ready(q, "q"), _ready(k, "k"), _ready(v, "v")
+    if k.shape != v.shape or q.shape[0] != k.shape[0] or q.shape[2:] != k.shape[2:]:
+        raise RuntimeError(f"solb200: dense_attn shapes q {tuple(q.shape)}, k {tuple(k.shape)}, "
+                           f"v {tuple(v.shape)}")
+    if not (q.device == k.device == v.device):
+        raise RuntimeError("solb200: q/k/v on different devices")
+    B, Tq, H, D = q.shape
+    Tk = k.shape[1]
+    scale = D ** -0.5 if scale is None else float(scale)
+    with torch.cuda.device(q.device):
+        ws = torch.empty(256, dtype=torch.uint8, device=q.device)
+        out = torch.empty((B, Tq, H, D), dtype=torch.bfloat16, device=q.device)
+        rc = lib().solb200_attn_dense(q.data_ptr(), _strides(q), k.data_ptr(), _strides(k), v.data_ptr(),
+                                      _strides(v), out.data_ptr(), B, Tq, Tk, H, D, scale, ws.data_ptr(), 256,
+                                      _stream_ptr(q.device))
+        check(rc, "dense_attn")
+        if _SYNC_CHECK:
+            code = c_int32(0)
+            check(lib().solb200_read_device_error(ws.data_ptr(), ctypes.byref(code), _stream_ptr(q.device)),
+                  "device error check")
+    return out
+
+
 def _tokens_check(q, tokens):
     if tokens is not None and int(tokens) != q.shape[1]:
         raise RuntimeError("solb200: tokens must equal q.shape[1] (inputs are never padded here)")

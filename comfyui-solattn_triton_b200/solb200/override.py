@@ -34,7 +34,8 @@ from . import ops
 HEAD_DIM = 128
 BLOCK_SIZE = 64          # routing block of the override (the reference's constant)
 
-_stats = {"sparse": 0, "dense_fallback": 0, "outside_range": 0, "dense_block": 0, "errors": 0}
+_stats = {"sparse": 0, "dense_fallback": 0, "outside_range": 0, "dense_block": 0, "errors": 0,
+          "dense_b200": 0}
 _seen = set()
 _probe = {}
 
@@ -130,6 +131,15 @@ def _ineligible(q, k, mask, dim_head, min_tokens):
     return None
 
 
+def _dense_capable(q, k, v, dim_head):
+    """Whether a declined BTHD call can run on the dense B200 kernel (``ops.dense_attn``)
+    instead of the host's attention: bf16 on an sm_100 device, head_dim 64 or 128, k and v
+    alike and q matching them in batch and heads (any sequence lengths)."""
+    return (q.device.type == "cuda" and q.dtype == k.dtype == v.dtype == torch.bfloat16
+            and dim_head in (64, 128) and k.shape == v.shape and q.shape[0] == k.shape[0]
+            and q.shape[2:] == k.shape[2:] and torch.cuda.get_device_capability(q.device)[0] == 10)
+
+
 def _run(q, k, v, heads, skip_reshape, skip_output_reshape, scale, tau, min_tokens, verbose,
          int8_qk=False, sink_blocks=(0, 0), sink_q=(0, 0), use_tma=False, int8_pv=True,
          block=BLOCK_SIZE):
@@ -143,6 +153,13 @@ def _run(q, k, v, heads, skip_reshape, skip_output_reshape, scale, tau, min_toke
         qs, ks, vs = (t.view(b, -1, heads, dim_head) for t in (q, k, v))
     reason = _ineligible(qs, ks, None, dim_head, min_tokens)
     if reason is not None:
+        if _dense_capable(qs, ks, vs, dim_head):
+            # this build's addition: the declined call runs dense on the same tensor cores
+            out = ops.dense_attn(qs, ks, vs, scale=scale)
+            _stats["dense_b200"] += 1
+            if verbose:
+                _log_once((tuple(qs.shape), reason, "b200"), f"dense sm_100a {tuple(qs.shape)}: {reason}")
+            return out.transpose(1, 2) if skip_output_reshape else out.reshape(b, -1, heads * dim_head)
         _stats["dense_fallback"] += 1
         if verbose:
             _log_once((tuple(qs.shape), reason), f"dense {tuple(qs.shape)}: {reason}")

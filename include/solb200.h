@@ -152,6 +152,19 @@ SOLB200_API int32_t solb200_sol_attn_reordered(const void* q, const int64_t* q_s
                                                const int64_t* order, int32_t int8, int32_t int8_pv,
                                                void* workspace, int64_t workspace_bytes, void* stream);
 
+/* Dense BF16 attention on the same tensor cores, for the calls the Sol-Attn path does not
+ * take (the reference hands them back to the host's attention, __init__.py:170-189,
+ * 271-279): softmax(q k^T * scale) v with every key block computed exactly, no routing.
+ * q: [batch, q_tokens, heads, head_dim], k/v: [batch, kv_tokens, heads, head_dim] (cross-
+ * attention when the lengths differ), bf16 with strides as above; head_dim 64 or 128; out:
+ * dense bf16 [batch, q_tokens, heads, head_dim]. workspace: >= 256 bytes (the device error
+ * word). No counterpart in the reference (it runs no kernel of its own for these calls). */
+SOLB200_API int32_t solb200_attn_dense(const void* q, const int64_t* q_strides, const void* k,
+                                       const int64_t* k_strides, const void* v, const int64_t* v_strides,
+                                       void* out, int64_t batch, int64_t q_tokens, int64_t kv_tokens,
+                                       int64_t heads, int64_t head_dim, float scale, void* workspace,
+                                       int64_t workspace_bytes, void* stream);
+
 /* BF16 Sol-Attn that allocates nothing, for hosts that cannot hand this library device
  * memory at call time (an application that plans all device allocations up front and
  * forbids allocating later, a plugin whose host owns the allocator, or a caller that
