@@ -247,7 +247,7 @@ def measure_c3(ctx, path, q, k, v, cfg):
 def int8_block(ctx, m, cfg, peaks):
     """The INT8 path's sub-object (config 3): ms per call, stage split, executed-op
     roofline of the forward kernel and the clocks of its timed region."""
-    achieved = m["flops_all"] / (m["ms_fwd"] * 1e-3) / 1e12
+    achieved = m["flops_all"] / ctx.world / (m["ms_fwd"] * 1e-3) / 1e12   # one GPU's launch
     return {
         "ms_per_call": m["ms"], "value": cfg.dense_flops() / (m["ms"] * 1e-3) / 1e12, "unit": UNIT,
         "stages_ms": {"prep_route": m["ms_prep"], "forward": m["ms_fwd"]},
@@ -256,8 +256,8 @@ def int8_block(ctx, m, cfg, peaks):
                      "unit": "TOP/s", "peak_bf16": peaks["bf16"], "frac_of_bf16_peak": achieved / peaks["bf16"],
                      "peak_int8": 2 * peaks["bf16"], "frac_of_int8_peak": achieved / (2 * peaks["bf16"]),
                      "traffic": profiled_traffic("int8", 40 // ctx.world),
-                     "note": "executed ops (int8 exact tiles + bf16 approximate tiles) per launch over "
-                             "all ranks / slowest rank's forward time; int8 peak = 2 x the measured "
+                     "note": "executed ops (int8 exact tiles + bf16 approximate tiles) of one GPU's launch "
+                             "(all ranks' / N) / the slowest rank's forward time; int8 peak = 2 x the measured "
                              f"bf16 peak (nominal ratio), {peaks['source']}"},
         "clocks": m["clocks"],
     }
@@ -455,7 +455,7 @@ def run_ours(args, rank, world, local_rank):
         torch.cuda.empty_cache()
         ulysses = {p: ulysses_block(ctx, p) for p in ("bf16", "int8")}
 
-    achieved = m["flops_all"] / (m["ms_fwd"] * 1e-3) / 1e12
+    achieved = m["flops_all"] / world / (m["ms_fwd"] * 1e-3) / 1e12   # one GPU's launch
     config = bench_config(args.path, world)
     if args.heads:
         config.update(workload=f"config3_video480p_B1_H{cfg.heads}_T32760_D128_blk128_tau0.9",
@@ -483,8 +483,8 @@ def run_ours(args, rank, world, local_rank):
                      "achieved": achieved, "peak": peaks["bf16"], "unit": "TFLOP/s",
                      "frac": achieved / peaks["bf16"],
                      "traffic": profiled_traffic(args.path, H),
-                     "note": f"executed flops {m['flops_all']:.4g} per launch over all ranks / the slowest "
-                             f"rank's forward kernel time (CUDA events on its stream); peak = bf16 dense "
+                     "note": f"executed flops of one GPU's launch ({m['flops_all']:.4g} over all ranks / {world}) "
+                             f"/ the slowest rank's forward kernel time (CUDA events on its stream); peak = bf16 dense "
                              f"burst, {peaks['source']}; traffic = DRAM bytes per launch from the ncu capture "
                              f"in profiles/, scaled to {H} heads"},
         "int8": int8,
