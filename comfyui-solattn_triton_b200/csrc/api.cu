@@ -231,8 +231,8 @@ int32_t run(const Plan& P, const Call& c) {
   pp.vc = at<__nv_bfloat16>(c.ws, P, SOLB200_BUF_VC);
   pp.centroid = at<float>(c.ws, P, SOLB200_BUF_CENTROID);
   pp.vamax = (c.int8 && c.int8_pv) ? at<float>(c.ws, P, SOLB200_BUF_VAMAX) : nullptr;
-  pp.qi = c.int8 ? at<int8_t>(c.ws, P, SOLB200_BUF_QI) : nullptr;
-  pp.qs = c.int8 ? at<float>(c.ws, P, SOLB200_BUF_QS) : nullptr;
+  int8_t* const qi_buf = c.int8 ? at<int8_t>(c.ws, P, SOLB200_BUF_QI) : nullptr;
+  float* const qs_buf = c.int8 ? at<float>(c.ws, P, SOLB200_BUF_QS) : nullptr;
   pp.perm = c.perm;
   pp.err = err;
   __nv_bfloat16* copies[3] = {nullptr, nullptr, nullptr};
@@ -241,8 +241,7 @@ int32_t run(const Plan& P, const Call& c) {
       copies[i] = reinterpret_cast<__nv_bfloat16*>(static_cast<char*>(c.ws) + P.off_copy[i]);
   pp.qcopy = copies[0]; pp.kcopy = copies[1]; pp.vcopy = copies[2];
   pp.B = (int)P.B; pp.T = (int)P.T; pp.H = (int)P.H; pp.N = P.N; pp.npad = P.npad; pp.blk = P.blk;
-  pp.tp = P.N * P.blk;
-  if (prep) launch_pool(pp, hd, pp.vamax != nullptr, c.int8, c.st);
+  if (prep) launch_pool(pp, hd, pp.vamax != nullptr, c.st);
 
   MomentsParams mp{};
   mp.kc = pp.kc;
@@ -255,18 +254,21 @@ int32_t run(const Plan& P, const Call& c) {
 
   if (c.int8 && prep) {
     QuantParams qp{};
-    qp.k = pp.k; qp.v = pp.v;
+    qp.q = pp.q; qp.k = pp.k; qp.v = pp.v;
+    qp.sq_b = pp.sq_b; qp.sq_t = pp.sq_t; qp.sq_h = pp.sq_h;
     qp.sk_b = pp.sk_b; qp.sk_t = pp.sk_t; qp.sk_h = pp.sk_h;
     qp.sv_b = pp.sv_b; qp.sv_t = pp.sv_t; qp.sv_h = pp.sv_h;
     qp.kmean = mp.kmean;
     qp.vscale = c.int8_pv ? mp.vscale : nullptr;
+    qp.qi = qi_buf;
+    qp.qs = qs_buf;
     qp.ki = at<int8_t>(c.ws, P, SOLB200_BUF_KI);
     qp.ks = at<float>(c.ws, P, SOLB200_BUF_KS);
     qp.vi = c.int8_pv ? at<int8_t>(c.ws, P, SOLB200_BUF_VI) : nullptr;
     qp.B = (int)P.B; qp.T = (int)P.T; qp.H = (int)P.H; qp.tp = P.N * P.blk;
     qp.perm = c.perm;
     qp.err = err;
-    launch_quant_kv(qp, hd, c.st);
+    launch_quant_qkv(qp, hd, c.st);
   }
 
   RouteParams rp{};
@@ -335,7 +337,7 @@ int32_t run(const Plan& P, const Call& c) {
     return SOLB200_OK;
   }
   // int8 operands: qi (128-row query tiles), ki and vi (one routed block per tile)
-  if ((rc = make_map(&m.qi, pp.qi, true, P.D, P.H, P.T, P.B, P.D, TD, P.T * TD, 128, "qi"))) return rc;
+  if ((rc = make_map(&m.qi, qi_buf, true, P.D, P.H, P.T, P.B, P.D, TD, P.T * TD, 128, "qi"))) return rc;
   if ((rc = make_map(&m.ki, at<int8_t>(c.ws, P, SOLB200_BUF_KI), true, P.D, P.H, P.T, P.B, P.D, TD, P.T * TD,
                      P.blk, "ki")))
     return rc;
@@ -346,7 +348,7 @@ int32_t run(const Plan& P, const Call& c) {
   } else {
     if ((rc = make_map(&m.v, vsrc, false, P.D, P.H, P.T, P.B, svm[2], svm[1], svm[0], kv_rows, "v"))) return rc;
   }
-  fp.qs = pp.qs;
+  fp.qs = qs_buf;
   fp.ks = at<float>(c.ws, P, SOLB200_BUF_KS);
   fp.vscale = mp.vscale;
   fp.int8_pv = c.int8_pv ? 1 : 0;

@@ -215,33 +215,6 @@ __device__ __forceinline__ float fast_exp2(float x) {
   return y;
 }
 
-// Packed fp32 pairs (Blackwell f32x2 FMA / add): one instruction for two lanes' worth
-// of arithmetic.
-__device__ __forceinline__ float2 fma2(float2 a, float2 b, float2 c) {
-  uint64_t r;
-  asm("fma.rn.f32x2 %0, %1, %2, %3;"
-      : "=l"(r)
-      : "l"(*reinterpret_cast<uint64_t*>(&a)), "l"(*reinterpret_cast<uint64_t*>(&b)),
-        "l"(*reinterpret_cast<uint64_t*>(&c)));
-  return *reinterpret_cast<float2*>(&r);
-}
-
-__device__ __forceinline__ float2 add2(float2 a, float2 b) {
-  uint64_t r;
-  asm("add.f32x2 %0, %1, %2;"
-      : "=l"(r)
-      : "l"(*reinterpret_cast<uint64_t*>(&a)), "l"(*reinterpret_cast<uint64_t*>(&b)));
-  return *reinterpret_cast<float2*>(&r);
-}
-
-__device__ __forceinline__ float2 mul2(float2 a, float2 b) {
-  uint64_t r;
-  asm("mul.f32x2 %0, %1, %2;"
-      : "=l"(r)
-      : "l"(*reinterpret_cast<uint64_t*>(&a)), "l"(*reinterpret_cast<uint64_t*>(&b)));
-  return *reinterpret_cast<float2*>(&r);
-}
-
 __device__ __forceinline__ float max3(float a, float b, float c) {
   float r;
   asm("max.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));

@@ -57,14 +57,6 @@ __device__ __forceinline__ uint32_t swz_off(int r, int c, int rb) {
   return rb == 128 ? (uint32_t)(r * 128 + ((c ^ (r & 7)) << 4)) : (uint32_t)(r * 64 + ((c ^ ((r >> 1) & 3)) << 4));
 }
 
-__device__ __forceinline__ float2 add_rz2(float2 a, float2 b) {
-  uint64_t r;
-  asm("add.rz.f32x2 %0, %1, %2;"
-      : "=l"(r)
-      : "l"(*reinterpret_cast<uint64_t*>(&a)), "l"(*reinterpret_cast<uint64_t*>(&b)));
-  return *reinterpret_cast<float2*>(&r);
-}
-
 // four int8 codes (low bytes of c[0..3]) in one word, c[0] lowest
 __device__ __forceinline__ uint32_t pack4(uint32_t c0, uint32_t c1, uint32_t c2, uint32_t c3) {
   uint32_t a, b, w;

@@ -1,11 +1,11 @@
 // Bandwidth-bound stages of the Sol-Attn path (sm_100a):
 //   pool_kernel      one pass over Q, K, V: kc (block mean of K), vc (block sum of V),
-//                    q-block centroids, optional per-block |V| max and per-token Q int8
+//                    q-block centroids, optional per-block |V| max
 //   moments_kernel   per (b, h): kc mean/variance (INT8: k_mean, kc centred in place,
 //                    V scales)
 //   route_kernel     per-q-block routing threshold, exact-block bitmask [B,H,N,NW],
 //                    counts, optional index lists
-//   quant_kv_kernel  per-token int8 of K - k_mean, per-channel int8 of V
+//   quant_qkv_kernel per-token int8 of Q and of K - k_mean, per-channel int8 of V
 //   morton kernels   Z-order ranks (no sort) and a row gather for the reorder
 //
 // Reductions that the reference performs in a defined order are done here in the
@@ -53,20 +53,6 @@ __device__ __forceinline__ float quotient_rn(float x, float s, float y) {
   return __fmaf_rn(__fmaf_rn(-s, q1, x), y, q1);
 }
 
-// The int8 code of q: round half away from zero as sign(q) * trunc(RN(|q| + 0.5)) (x + 0.5
-// rounded, then truncated: the arithmetic of the reference's conversion), clamped to
-// +-127; returned in the low byte (two's complement). Clamping |q| to 127 first gives
-// the same code whether the reference clamps before rounding (_fused_prep.py) or after
-// (_fused_quant.py): rounding is monotonic and maps 127 to 127. trunc(w), w in
-// [0.5, 127.5], is read from the bits of w + 2^23 added with rounding toward zero (an
-// FMA-pipe add instead of the conversion unit); the sign is applied as (m ^ s) - s.
-__device__ __forceinline__ uint32_t code_byte(float q) {
-  const float w = __fadd_rn(fminf(fabsf(q), 127.f), 0.5f);
-  const uint32_t m = __float_as_uint(__fadd_rz(w, 8388608.f));   // 2^23 + trunc(w)
-  const uint32_t sgn = (uint32_t)((int32_t)__float_as_uint(q) >> 31);
-  return (m ^ sgn) - sgn;
-}
-
 // eight int8 codes (low bytes of c[0..7]) packed into two words, c[0] lowest
 __device__ __forceinline__ uint2 pack_codes(const uint32_t (&c)[8]) {
   uint32_t a, b, lo, hi;
@@ -80,19 +66,19 @@ __device__ __forceinline__ uint2 pack_codes(const uint32_t (&c)[8]) {
 }
 
 // One thread owns 8 consecutive channels (16 bytes) of one head and one of the three
-// tensors (role 0: Q -> centroid and, for INT8, qi / qs; role 1: K -> kc; role 2:
+// tensors (role 0: Q -> centroid; role 1: K -> kc; role 2:
 // V -> vc and |V| max), so a call with few heads still has three threads per channel
 // group in flight. Rows are accumulated in token order (row 0 first) in fp32, the
 // order of the reference's block sums; the loads of ROWS rows are issued before any of
 // them is added, so a thread keeps ROWS x 16 bytes in flight.
-// Grid: (3*ceil(H*D/8 / NT), Npad, B), role = blockIdx.x % 3 so that the three roles (the
-// Q role carries the INT8 quantisation) interleave in launch order; NT = 32 or 64
-// threads (launch_pool_t).
-template <int HD, bool VAMAX, bool QQUANT>
+// Grid: (3*ceil(H*D/8 / NT), Npad, B), role = blockIdx.x % 3 so that the three roles
+// interleave in launch order; NT = 32 or 64 threads (launch_pool_t). The INT8 codes of
+// Q are formed by quant_qkv_kernel, with those of K and V.
+template <int HD, bool VAMAX>
 __global__ void __launch_bounds__(64) pool_kernel(PoolParams p) {
   pdl_begin();
   constexpr int LANES_PER_HEAD = HD / 8;
-  constexpr int ROWS = (VAMAX || QQUANT) ? 8 : 16;   // the INT8 variants keep fewer rows in registers
+  constexpr int ROWS = 16;
   const int g = (blockIdx.x / 3) * blockDim.x + threadIdx.x;
   const int n = blockIdx.y, role = blockIdx.x % 3, b = blockIdx.z;
   const bool active = g < p.H * LANES_PER_HEAD;
@@ -160,27 +146,6 @@ __global__ void __launch_bounds__(64) pool_kernel(PoolParams p) {
       if (VAMAX && role == 2) {
 #pragma unroll
         for (int i = 0; i < 8; ++i) vmax[i] = fmaxf(vmax[i], fabsf(x[i]));
-      }
-      if (QQUANT && role == 0) {
-        // per-token symmetric int8 of Q (_fused_prep.py:36-44): s = max|x| / 127,
-        // floor at 1e-8, clamp(x / s, +-127), round half away from zero.
-        float amax = 0.f;
-#pragma unroll
-        for (int i = 0; i < 8; ++i) amax = fmaxf(amax, fabsf(x[i]));
-#pragma unroll
-        for (int off = 1; off < LANES_PER_HEAD; off <<= 1)
-          amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, off));
-        const float s = __fdiv_rn(amax, 127.f);
-        const float s_safe = s > 1e-8f ? s : 1e-8f;
-        const float y = __frcp_rn(s_safe);
-        if (active) {
-          uint32_t c[8];
-#pragma unroll
-          for (int i = 0; i < 8; ++i) c[i] = code_byte(quotient_rn(x[i], s_safe, y));
-          const int64_t qo = (((int64_t)b * p.T + r) * p.H + h) * HD + d0;
-          *reinterpret_cast<uint2*>(p.qi + qo) = pack_codes(c);
-          if (d0 == 0) p.qs[((int64_t)b * p.H + h) * p.tp + r] = s_safe;
-        }
       }
     }
   }
@@ -573,21 +538,45 @@ __global__ void __launch_bounds__(256) route_kernel(RouteParams p) {
   }
 }
 
-// ---------------------------------------------------------------- quant K, V
+// ------------------------------------------------------------- quant Q, K, V
 
-
-// K: per-(token, head) int8 of K - k_mean (_fused_quant.py:8-42): s = max|x|/127,
-//    floor 1e-8, round half away from zero of x/s, clamp +-127.
+// Q: per-(token, head) symmetric int8 (_fused_prep.py:36-44); K: per-(token, head) int8 of
+//    K - k_mean (_fused_quant.py:8-42); both s = max|x| / 127, floor 1e-8, round half away
+//    from zero of x / s (the clamp to +-127 never acts, see code_pair).
 // V: per-channel int8 with the (b, h, d) scale (_fused_quant.py:61-88).
-// One thread per 8 channels of a (head, group of TOK consecutive tokens); a head's lanes
-// share a warp. The K and V rows of all TOK tokens are loaded before any is quantised.
-constexpr int kQuantTok = 2;
+// One thread per 8 channels of a (head, group of kQuantTok consecutive tokens); a head's
+// lanes share a warp. The quotients are formed two lanes at a time (f32x2), with the same
+// IEEE operations as quotient_rn.
+constexpr int kQuantTok = 2, kQuantStages = 4;
 
-// int8 codes clamp(round half away from zero of x / den, +-127); rcp = RN(1 / den)
+// quotient_rn of two values at once
+__device__ __forceinline__ float2 quotient_rn2(float2 x, float2 s, float2 y) {
+  const float2 ns = make_float2(-s.x, -s.y);
+  const float2 q0 = mul2(x, y);
+  const float2 q1 = fma2(fma2(ns, q0, x), y, q0);
+  return fma2(fma2(ns, q1, x), y, q1);
+}
+
+// The int8 codes of two quotients, round half away from zero: trunc(RN(q + copysign(0.5,
+// q))), the arithmetic of the reference's conversion (x / s, then + or - 0.5, then a
+// truncating cast), as two's-complement words (the code in the low byte). Valid for
+// |q| <= 127.5, where clamping to +-127 (the reference's, before or after rounding) changes
+// nothing: the quantisers divide by s >= max|x| / 127 (rounded), so |q| <= 127 (1 + 2^-23).
+__device__ __forceinline__ void code_pair(float2 q, uint32_t& c0, uint32_t& c1) {
+  const float2 v = add2(q, make_float2(copysignf(0.5f, q.x), copysignf(0.5f, q.y)));
+  c0 = (uint32_t)__float2int_rz(v.x);
+  c1 = (uint32_t)__float2int_rz(v.y);
+}
+
+// int8 codes round half away from zero of x / den (|x| <= 127 den, see code_pair);
+// rcp = RN(1 / den)
 __device__ __forceinline__ uint2 quant8(const float (&x)[8], const float (&den)[8], const float (&rcp)[8]) {
   uint32_t c[8];
 #pragma unroll
-  for (int i = 0; i < 8; ++i) c[i] = code_byte(quotient_rn(x[i], den[i], rcp[i]));
+  for (int i = 0; i < 8; i += 2)
+    code_pair(quotient_rn2(make_float2(x[i], x[i + 1]), make_float2(den[i], den[i + 1]),
+                             make_float2(rcp[i], rcp[i + 1])),
+                c[i], c[i + 1]);
   return pack_codes(c);
 }
 
@@ -601,105 +590,185 @@ __device__ __forceinline__ void unpack8(const uint4& u, float (&x)[8]) {
   }
 }
 
-template <int HD>
-__global__ void __launch_bounds__(256, 3) quant_kv_kernel(QuantParams p) {
-  pdl_begin();
-  constexpr int LPH = HD / 8, TOK = kQuantTok;
-  const int64_t per_grp = (int64_t)p.H * LPH;
-  const int64_t groups = (p.T + TOK - 1) / TOK;
-  const int64_t gid = (int64_t)blockIdx.x * 256 + threadIdx.x;
-  const bool active = gid < (int64_t)p.B * groups * per_grp;
-  const int64_t g = active ? gid : 0;
-  const int b = (int)(g / (groups * per_grp));
-  const int64_t rem = g - (int64_t)b * groups * per_grp;
-  const int t0 = (int)(rem / per_grp) * TOK;
-  const int hl = (int)(rem % per_grp);
-  const int h = hl / LPH, d0 = (hl % LPH) * 8;
-  const bool with_v = p.vi != nullptr;
-  uint4 uk[TOK], uv[TOK];
+// Per-(token, head) codes of this lane's 8 values: the head's max |x| over its LPH lanes,
+// s = max(RN(max / 127), 1e-8) (returned), codes of x / s.
+template <int LPH>
+__device__ __forceinline__ uint2 token_codes(const float (&x)[8], float& s_out) {
+  float amax = 0.f;
 #pragma unroll
-  for (int i = 0; i < TOK; ++i) {
-    const bool ok = active && t0 + i < p.T;
-    const int t = ok ? t0 + i : 0;
-    const int64_t src_t = ok ? order_row(p.perm, t, p.T, p.err) : 0;   // token of row t
-    uk[i] = ok ? __ldg(reinterpret_cast<const uint4*>(p.k + (int64_t)b * p.sk_b + src_t * p.sk_t +
-                                                      (int64_t)h * p.sk_h + d0))
-               : make_uint4(0, 0, 0, 0);
-    uv[i] = ok && with_v ? __ldg(reinterpret_cast<const uint4*>(p.v + (int64_t)b * p.sv_b + src_t * p.sv_t +
-                                                               (int64_t)h * p.sv_h + d0))
-                         : make_uint4(0, 0, 0, 0);
+  for (int c = 0; c < 8; ++c) amax = fmaxf(amax, fabsf(x[c]));
+#pragma unroll
+  for (int off = 1; off < LPH; off <<= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, off));
+  // RN(amax / 127) by quotient_rn with RN(1 / 127): exact for every amax that is not
+  // subnormal, and a subnormal amax gives s < 1e-8, replaced by the floor below
+  const float s = quotient_rn(amax, 127.f, 0.007874015718698502f);
+  const float s_safe = s > 1e-8f ? s : 1e-8f;
+  const float y = __frcp_rn(s_safe);
+  float den[8], rcp[8];
+#pragma unroll
+  for (int c = 0; c < 8; ++c) {
+    den[c] = s_safe;
+    rcp[c] = y;
   }
-  float m[8], sc[8];
-  {
-    const float4* mp = reinterpret_cast<const float4*>(p.kmean + ((int64_t)b * p.H + h) * HD + d0);
-    const float4 m0 = __ldg(mp), m1 = __ldg(mp + 1);
-    m[0] = m0.x; m[1] = m0.y; m[2] = m0.z; m[3] = m0.w; m[4] = m1.x; m[5] = m1.y; m[6] = m1.z; m[7] = m1.w;
-    if (with_v) {
-      const float4* sp = reinterpret_cast<const float4*>(p.vscale + ((int64_t)b * p.H + h) * HD + d0);
-      const float4 s0 = __ldg(sp), s1 = __ldg(sp + 1);
-      sc[0] = s0.x; sc[1] = s0.y; sc[2] = s0.z; sc[3] = s0.w; sc[4] = s1.x; sc[5] = s1.y; sc[6] = s1.z; sc[7] = s1.w;
-    }
-  }
-  float sc_rcp[8];
-#pragma unroll
-  for (int c = 0; c < 8; ++c) sc_rcp[c] = with_v ? __frcp_rn(sc[c]) : 0.f;
-#pragma unroll
-  for (int i = 0; i < TOK; ++i) {
-    const int t = t0 + i;
-    const bool ok = active && t < p.T;
-    float xk[8], den[8];
-    unpack8(uk[i], xk);
-    float amax = 0.f;
-#pragma unroll
-    for (int c = 0; c < 8; ++c) {
-      xk[c] = __fsub_rn(xk[c], m[c]);
-      amax = fmaxf(amax, fabsf(xk[c]));
-    }
-#pragma unroll
-    for (int off = 1; off < LPH; off <<= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, off));
-    const float s = __fdiv_rn(amax, 127.f);
-    const float s_safe = s > 1e-8f ? s : 1e-8f;
-    const float y = __frcp_rn(s_safe);
-    float rcp[8];
-#pragma unroll
-    for (int c = 0; c < 8; ++c) {
-      den[c] = s_safe;
-      rcp[c] = y;
-    }
-    const int64_t o = (((int64_t)b * p.T + t) * p.H + h) * HD + d0;
-    const uint2 qk = quant8(xk, den, rcp);
-    if (ok) {
-      *reinterpret_cast<uint2*>(p.ki + o) = qk;
-      if (d0 == 0) p.ks[((int64_t)b * p.H + h) * p.tp + t] = s_safe;
-    }
-    if (with_v) {
-      float xv[8];
-      unpack8(uv[i], xv);
-      const uint2 qv = quant8(xv, sc, sc_rcp);
-      if (ok) *reinterpret_cast<uint2*>(p.vi + o) = qv;
-    }
-  }
+  s_out = s_safe;
+  return quant8(x, den, rcp);
 }
 
-// Self-test of quotient_rn and code_byte against CUDA's IEEE division and
-// conversion on caller-given (x, s) pairs: counts the pairs whose quotient differs in
-// value from __fdiv_rn(x, s) (bad[0]) and whose int8 code (clamp after rounding, as
-// quant8) differs (bad[1]).
+// 16-byte cp.async that reads `src_bytes` (16 or 0: zero fill) from gmem
+__device__ __forceinline__ void cp_async16_zfill(uint32_t smem_addr, const void* gmem, uint32_t src_bytes) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(smem_addr), "l"(gmem), "r"(src_bytes)
+               : "memory");
+}
+
+// Grid layout of quant_qkv_kernel: a stripe of kQuantStripeCtas(per_grp) CTAs covers whole
+// token groups (lcm(per_grp, 256) threads), so a thread keeps one (head, 8-channel) lane
+// for all the token groups it visits, stepping by the grid's stripes.
+static inline int64_t quant_stripe_threads(int64_t per_grp) {
+  int64_t a = per_grp, b = 256;
+  while (b) {
+    const int64_t t = a % b;
+    a = b;
+    b = t;
+  }
+  return per_grp / a * 256;   // lcm(per_grp, 256)
+}
+
+// Persistent form: each thread walks its token groups with kQuantStages groups of Q / K /
+// V rows in flight (cp.async into its own shared-memory slots; no thread reads another's),
+// and quantises one group while the next ones load.
+template <int HD>
+__global__ void __launch_bounds__(256, 2) quant_qkv_kernel(QuantParams p, int stripe_ctas) {
+  pdl_begin();
+  constexpr int LPH = HD / 8, TOK = kQuantTok, NS = kQuantStages, SLOTS = 3 * TOK;
+  extern __shared__ __align__(16) uint4 qbuf[];   // [NS][SLOTS][256]
+  const int64_t per_grp = (int64_t)p.H * LPH;
+  const int64_t groups = (p.T + TOK - 1) / TOK;
+  const int64_t total_bg = (int64_t)p.B * groups;
+  const int64_t stripe_threads = (int64_t)stripe_ctas * 256;
+  const int64_t stripe_groups = stripe_threads / per_grp;
+  const int64_t lin = (int64_t)(blockIdx.x % stripe_ctas) * 256 + threadIdx.x;
+  const int hl = (int)(lin % per_grp);
+  const int h = hl / LPH, d0 = (hl % LPH) * 8;
+  const int64_t bg0 = (int64_t)(blockIdx.x / stripe_ctas) * stripe_groups;   // the CTA's first group row
+  const int64_t gi = lin / per_grp;
+  const int64_t step = (int64_t)(gridDim.x / stripe_ctas) * stripe_groups;
+  const bool with_q = p.qi != nullptr, with_v = p.vi != nullptr;
+  const uint32_t base = smem_u32(qbuf) + threadIdx.x * 16;
+  // loads of the k-th group this thread visits into stage k % NS (zero rows past the end)
+  auto issue = [&](int64_t k) {
+    const int64_t bg = bg0 + gi + k * step;
+    const uint32_t sb = base + (uint32_t)((k % NS) * SLOTS * 256 * 16);
+    const int b = (int)(bg < total_bg ? bg / groups : 0);
+    const int t0 = (int)(bg < total_bg ? bg % groups : 0) * TOK;
+#pragma unroll
+    for (int i = 0; i < TOK; ++i) {
+      const bool ok = bg < total_bg && t0 + i < p.T;
+      const int64_t src_t = ok ? order_row(p.perm, t0 + i, p.T, p.err) : 0;
+      const __nv_bfloat16* q = p.q + (int64_t)b * p.sq_b + src_t * p.sq_t + (int64_t)h * p.sq_h + d0;
+      const __nv_bfloat16* k_ = p.k + (int64_t)b * p.sk_b + src_t * p.sk_t + (int64_t)h * p.sk_h + d0;
+      const __nv_bfloat16* v = p.v + (int64_t)b * p.sv_b + src_t * p.sv_t + (int64_t)h * p.sv_h + d0;
+      cp_async16_zfill(sb + (0 * TOK + i) * 256 * 16, q, ok && with_q ? 16u : 0u);
+      cp_async16_zfill(sb + (1 * TOK + i) * 256 * 16, k_, ok ? 16u : 0u);
+      cp_async16_zfill(sb + (2 * TOK + i) * 256 * 16, v, ok && with_v ? 16u : 0u);
+    }
+  };
+  // number of groups this CTA's threads visit (uniform over the CTA, so every lane of a
+  // head takes part in every shuffle)
+  const int64_t nk = bg0 < total_bg ? (total_bg - bg0 + step - 1) / step : 0;
+#pragma unroll
+  for (int s = 0; s < NS - 1; ++s) {
+    if (s < nk) issue(s);
+    asm volatile("cp.async.commit_group;" ::: "memory");
+  }
+  int cur_b = -1;
+  float m[8], sc[8], sc_rcp[8];
+  for (int64_t k = 0; k < nk; ++k) {
+    if (k + NS - 1 < nk) issue(k + NS - 1);
+    asm volatile("cp.async.commit_group;" ::: "memory");
+    asm volatile("cp.async.wait_group %0;" ::"n"(NS - 1) : "memory");
+    const int64_t bg = bg0 + gi + k * step;
+    const bool live = bg < total_bg;
+    const int b = (int)(live ? bg / groups : 0);
+    const int t0 = (int)(live ? bg % groups : 0) * TOK;
+    if (b != cur_b) {   // per-(b, h) constants of this lane
+      cur_b = b;
+      const float4* mp = reinterpret_cast<const float4*>(p.kmean + ((int64_t)b * p.H + h) * HD + d0);
+      const float4 m0 = __ldg(mp), m1 = __ldg(mp + 1);
+      m[0] = m0.x; m[1] = m0.y; m[2] = m0.z; m[3] = m0.w; m[4] = m1.x; m[5] = m1.y; m[6] = m1.z; m[7] = m1.w;
+      if (with_v) {
+        const float4* sp = reinterpret_cast<const float4*>(p.vscale + ((int64_t)b * p.H + h) * HD + d0);
+        const float4 s0 = __ldg(sp), s1 = __ldg(sp + 1);
+        sc[0] = s0.x; sc[1] = s0.y; sc[2] = s0.z; sc[3] = s0.w; sc[4] = s1.x; sc[5] = s1.y; sc[6] = s1.z; sc[7] = s1.w;
+      }
+#pragma unroll
+      for (int c = 0; c < 8; ++c) sc_rcp[c] = with_v ? __frcp_rn(sc[c]) : 0.f;
+    }
+    const uint4* sl = qbuf + (k % NS) * SLOTS * 256 + threadIdx.x;
+#pragma unroll
+    for (int i = 0; i < TOK; ++i) {
+      const int t = t0 + i;
+      const bool ok = live && t < p.T;
+      const int64_t o = (((int64_t)b * p.T + t) * p.H + h) * HD + d0;
+      const int64_t so = ((int64_t)b * p.H + h) * p.tp + t;
+      if (with_q) {
+        float xq[8], s;
+        unpack8(sl[(0 * TOK + i) * 256], xq);
+        const uint2 cq = token_codes<LPH>(xq, s);
+        if (ok) {
+          *reinterpret_cast<uint2*>(p.qi + o) = cq;
+          if (d0 == 0) p.qs[so] = s;
+        }
+      }
+      {
+        float xk[8], s;
+        unpack8(sl[(1 * TOK + i) * 256], xk);
+#pragma unroll
+        for (int c = 0; c < 8; ++c) xk[c] = __fsub_rn(xk[c], m[c]);
+        const uint2 ck = token_codes<LPH>(xk, s);
+        if (ok) {
+          *reinterpret_cast<uint2*>(p.ki + o) = ck;
+          if (d0 == 0) p.ks[so] = s;
+        }
+      }
+      if (with_v) {
+        float xv[8];
+        unpack8(sl[(2 * TOK + i) * 256], xv);
+        const uint2 cv = quant8(xv, sc, sc_rcp);
+        if (ok) *reinterpret_cast<uint2*>(p.vi + o) = cv;
+      }
+    }
+  }
+  asm volatile("cp.async.wait_all;" ::: "memory");
+}
+
+// Self-test of the quantisers' arithmetic against CUDA's IEEE division and conversion on
+// caller-given (x, s) pairs, two at a time as in quant8: counts the pairs whose quotient
+// (quotient_rn2) differs in value from __fdiv_rn(x, s) (bad[0]) and whose int8 code
+// (code_pair of the quotient clamped to +-127, which equals the reference's clamp after
+// rounding for any quotient) differs (bad[1]).
 __global__ void __launch_bounds__(256) quotient_selftest_kernel(const float* __restrict__ x,
                                                                 const float* __restrict__ s, int64_t n,
                                                                 unsigned long long* bad) {
   pdl_begin();
   unsigned long long nq = 0, nc = 0;
-  for (int64_t i = (int64_t)blockIdx.x * 256 + threadIdx.x; i < n; i += (int64_t)gridDim.x * 256) {
-    const float xi = x[i], si = s[i];
-    const float want = __fdiv_rn(xi, si);
-    const float got = quotient_rn(xi, si, __frcp_rn(si));
-    if (!(got == want)) ++nq;
-    const float wc = fminf(fmaxf(want, -256.f), 256.f);
-    const int want_code = max(-127, min(127, wc >= 0.f ? __float2int_rz(__fadd_rn(wc, 0.5f))
-                                                       : __float2int_rz(__fsub_rn(wc, 0.5f))));
-    const int got_code = (int)(int8_t)(code_byte(got) & 0xffu);
-    if (got_code != want_code) ++nc;
+  const int64_t pairs = (n + 1) / 2;
+  for (int64_t i = (int64_t)blockIdx.x * 256 + threadIdx.x; i < pairs; i += (int64_t)gridDim.x * 256) {
+    const int64_t i0 = 2 * i, i1 = 2 * i + 1 < n ? 2 * i + 1 : 2 * i;
+    const float2 xi = make_float2(x[i0], x[i1]), si = make_float2(s[i0], s[i1]);
+    const float2 got = quotient_rn2(xi, si, make_float2(__frcp_rn(si.x), __frcp_rn(si.y)));
+    uint32_t c[2];
+    code_pair(make_float2(fminf(fmaxf(got.x, -127.f), 127.f), fminf(fmaxf(got.y, -127.f), 127.f)), c[0], c[1]);
+    const float g2[2] = {got.x, got.y}, x2[2] = {xi.x, xi.y}, s2[2] = {si.x, si.y};
+#pragma unroll
+    for (int e = 0; e < 2; ++e) {
+      if (e == 1 && i1 == i0) break;
+      const float want = __fdiv_rn(x2[e], s2[e]);
+      if (!(g2[e] == want)) ++nq;
+      const float wc = fminf(fmaxf(want, -256.f), 256.f);
+      const int want_code = max(-127, min(127, wc >= 0.f ? __float2int_rz(__fadd_rn(wc, 0.5f))
+                                                         : __float2int_rz(__fsub_rn(wc, 0.5f))));
+      if ((int)(int8_t)(c[e] & 0xffu) != want_code) ++nc;
+    }
   }
   if (nq) atomicAdd(bad, nq);
   if (nc) atomicAdd(bad + 1, nc);
@@ -802,20 +871,18 @@ __global__ void __launch_bounds__(256) gather_rows_kernel(GatherParams p) {
 // ------------------------------------------------------------- host launches
 
 template <int HD>
-static void launch_pool_t(const PoolParams& p, bool vamax, bool qquant, cudaStream_t st) {
+static void launch_pool_t(const PoolParams& p, bool vamax, cudaStream_t st) {
   // 64-thread CTAs when the channel groups fill them, else 32 (fewer idle lanes at small H)
   const int lanes = p.H * (HD / 8);
   const int nt = lanes % 64 == 0 ? 64 : 32;
   dim3 grid(3 * ((lanes + nt - 1) / nt), p.npad, p.B);
-  if (vamax && qquant) launch_pdl(pool_kernel<HD, true, true>, grid, dim3(nt), 0, st, p);
-  else if (vamax) launch_pdl(pool_kernel<HD, true, false>, grid, dim3(nt), 0, st, p);
-  else if (qquant) launch_pdl(pool_kernel<HD, false, true>, grid, dim3(nt), 0, st, p);
-  else launch_pdl(pool_kernel<HD, false, false>, grid, dim3(nt), 0, st, p);
+  if (vamax) launch_pdl(pool_kernel<HD, true>, grid, dim3(nt), 0, st, p);
+  else launch_pdl(pool_kernel<HD, false>, grid, dim3(nt), 0, st, p);
 }
 
-void launch_pool(const PoolParams& p, int hd, bool vamax, bool qquant, cudaStream_t st) {
-  if (hd == 128) launch_pool_t<128>(p, vamax, qquant, st);
-  else launch_pool_t<64>(p, vamax, qquant, st);
+void launch_pool(const PoolParams& p, int hd, bool vamax, cudaStream_t st) {
+  if (hd == 128) launch_pool_t<128>(p, vamax, st);
+  else launch_pool_t<64>(p, vamax, st);
 }
 
 template <int HD, bool INT8>
@@ -910,11 +977,28 @@ void launch_route(const RouteParams& p, int hd, cudaStream_t st) {
   else launch_route_t<64>(p, st);
 }
 
-void launch_quant_kv(const QuantParams& p, int hd, cudaStream_t st) {
-  const int64_t total = (int64_t)p.B * ((p.T + kQuantTok - 1) / kQuantTok) * p.H * (hd / 8);
-  const int64_t grid = (total + 255) / 256;
-  if (hd == 128) launch_pdl(quant_kv_kernel<128>, dim3((unsigned)grid), dim3(256), 0, st, p);
-  else launch_pdl(quant_kv_kernel<64>, dim3((unsigned)grid), dim3(256), 0, st, p);
+void launch_quant_qkv(const QuantParams& p, int hd, cudaStream_t st) {
+  static int sms = 0;   // SM count of the device (same on every GPU of a node)
+  if (sms == 0) {
+    int dev = 0, n = 0;
+    cudaGetDevice(&dev);
+    sms = cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) == cudaSuccess && n > 0 ? n : 148;
+  }
+  const int64_t per_grp = (int64_t)p.H * (hd / 8);
+  const int stripe_ctas = (int)(quant_stripe_threads(per_grp) / 256);
+  const int64_t total_bg = (int64_t)p.B * ((p.T + kQuantTok - 1) / kQuantTok);
+  const int64_t stripe_groups = quant_stripe_threads(per_grp) / per_grp;
+  int64_t stripes = std::max<int64_t>(1, (2 * (int64_t)sms) / stripe_ctas);   // two CTAs per SM
+  stripes = std::min<int64_t>(stripes, (total_bg + stripe_groups - 1) / stripe_groups);
+  const dim3 grid((unsigned)(stripes * stripe_ctas));
+  const size_t smem = (size_t)kQuantStages * 3 * kQuantTok * 256 * 16;
+  if (hd == 128) {
+    cudaFuncSetAttribute(quant_qkv_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    launch_pdl(quant_qkv_kernel<128>, grid, dim3(256), smem, st, p, stripe_ctas);
+  } else {
+    cudaFuncSetAttribute(quant_qkv_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    launch_pdl(quant_qkv_kernel<64>, grid, dim3(256), smem, st, p, stripe_ctas);
+  }
 }
 
 void launch_morton(int64_t frames, int64_t height, int64_t width, int curve, int64_t roll,

@@ -11,14 +11,12 @@ struct PoolParams {
   __nv_bfloat16* kc; __nv_bfloat16* vc;      // [B, Npad, H, D]
   float* centroid;                            // [B, N, H, D]
   float* vamax;                               // [B, N, H, D] or null
-  int8_t* qi;                                 // [B, T, H, D] or null
-  float* qs;                                  // [B, H, tp] or null
   // token order (reordered calls): row r of every tensor is input token perm[r]; the
   // rows are also written, in that order, to the dense copies that are non-null
   const int64_t* perm;                        // [T] or null
   __nv_bfloat16* qcopy; __nv_bfloat16* kcopy; __nv_bfloat16* vcopy;   // [B, T, H, D] or null
   int* err;                                   // device error word (perm index out of range)
-  int B, T, H, N, npad, blk, tp;              // tp = N * blk (row stride of qs)
+  int B, T, H, N, npad, blk;
 };
 
 struct MomentsParams {
@@ -47,10 +45,11 @@ struct RouteParams {
 };
 
 struct QuantParams {
-  const __nv_bfloat16* k; const __nv_bfloat16* v;
-  int64_t sk_b, sk_t, sk_h, sv_b, sv_t, sv_h;
+  const __nv_bfloat16* q; const __nv_bfloat16* k; const __nv_bfloat16* v;
+  int64_t sq_b, sq_t, sq_h, sk_b, sk_t, sk_h, sv_b, sv_t, sv_h;
   const float* kmean;    // [B, H, D]
   const float* vscale;   // [B, H, D] or null
+  int8_t* qi; float* qs; // [B, T, H, D], [B, H, tp]
   int8_t* ki; float* ks; // [B, T, H, D], [B, H, tp]
   int8_t* vi;            // [B, T, H, D] or null
   const int64_t* perm;   // [T] token order (reordered calls) or null
@@ -67,12 +66,12 @@ struct GatherParams {
   int64_t batch, rows, row_bytes;
 };
 
-void launch_pool(const PoolParams& p, int hd, bool vamax, bool qquant, cudaStream_t st);
+void launch_pool(const PoolParams& p, int hd, bool vamax, cudaStream_t st);
 void launch_moments(const MomentsParams& p, int hd, bool int8, cudaStream_t st);
 void launch_route(const RouteParams& p, int hd, cudaStream_t st);
 // order[bh*N ..] = the units of head bh, its query blocks by descending count
 void launch_order(const int* count, int* order, int bh_count, int n, cudaStream_t st);
-void launch_quant_kv(const QuantParams& p, int hd, cudaStream_t st);
+void launch_quant_qkv(const QuantParams& p, int hd, cudaStream_t st);
 void launch_morton(int64_t frames, int64_t height, int64_t width, int curve, int64_t roll,
                    int64_t* perm, int64_t* inverse, cudaStream_t st);
 void launch_gather(const GatherParams& p, cudaStream_t st);

@@ -1,9 +1,10 @@
 """The int8 quantisers divide without a division per element (one correctly rounded
-reciprocal per scale, then two FMA remainder corrections: Markstein's theorem) and round
-half away from zero without the conversion unit. These tests compare both, on the GPU,
-with CUDA's IEEE division __fdiv_rn and its truncating conversion, through the library's
-self-test entry point: random pairs over the scale range the quantisers use, the exact
-tie points (k + 0.5) * s and their neighbours, and edge scales."""
+reciprocal per scale, then two FMA remainder corrections: Markstein's theorem, two lanes
+at a time) and round half away from zero as x / s + copysign(0.5) then a truncating
+conversion. These tests compare both, on the GPU, with CUDA's IEEE division __fdiv_rn and
+the reference's rounding, through the library's self-test entry point: random pairs over
+the scale range the quantisers use, the exact tie points (k + 0.5) * s and their
+neighbours, and edge scales."""
 
 import numpy as np
 import pytest
