@@ -544,10 +544,10 @@ __global__ void __launch_bounds__(256) route_kernel(RouteParams p) {
 //    K - k_mean (_fused_quant.py:8-42); both s = max|x| / 127, floor 1e-8, round half away
 //    from zero of x / s (the clamp to +-127 never acts, see code_pair).
 // V: per-channel int8 with the (b, h, d) scale (_fused_quant.py:61-88).
-// One thread per 8 channels of a (head, group of kQuantTok consecutive tokens); a head's
-// lanes share a warp. The quotients are formed two lanes at a time (f32x2), with the same
-// IEEE operations as quotient_rn.
-constexpr int kQuantTok = 2, kQuantStages = 4;
+// One thread per 16 channels of a (head, token); a head's lanes share a warp. The
+// quotients are formed two lanes at a time (f32x2), with the same IEEE operations as
+// quotient_rn.
+constexpr int kQuantStages = 4;
 
 // quotient_rn of two values at once
 __device__ __forceinline__ float2 quotient_rn2(float2 x, float2 s, float2 y) {
@@ -590,13 +590,13 @@ __device__ __forceinline__ void unpack8(const uint4& u, float (&x)[8]) {
   }
 }
 
-// Per-(token, head) codes of this lane's 8 values: the head's max |x| over its LPH lanes,
+// Per-(token, head) codes of this lane's 16 values: the head's max |x| over its LPH lanes,
 // s = max(RN(max / 127), 1e-8) (returned), codes of x / s.
 template <int LPH>
-__device__ __forceinline__ uint2 token_codes(const float (&x)[8], float& s_out) {
+__device__ __forceinline__ uint4 token_codes(const float (&x)[16], float& s_out) {
   float amax = 0.f;
 #pragma unroll
-  for (int c = 0; c < 8; ++c) amax = fmaxf(amax, fabsf(x[c]));
+  for (int c = 0; c < 16; ++c) amax = fmaxf(amax, fabsf(x[c]));
 #pragma unroll
   for (int off = 1; off < LPH; off <<= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, off));
   // RN(amax / 127) by quotient_rn with RN(1 / 127): exact for every amax that is not
@@ -611,7 +611,10 @@ __device__ __forceinline__ uint2 token_codes(const float (&x)[8], float& s_out) 
     rcp[c] = y;
   }
   s_out = s_safe;
-  return quant8(x, den, rcp);
+  const float(&lo)[8] = *reinterpret_cast<const float(*)[8]>(&x[0]);
+  const float(&hi)[8] = *reinterpret_cast<const float(*)[8]>(&x[8]);
+  const uint2 a = quant8(lo, den, rcp), b = quant8(hi, den, rcp);
+  return make_uint4(a.x, a.y, b.x, b.y);
 }
 
 // 16-byte cp.async that reads `src_bytes` (16 or 0: zero fill) from gmem
@@ -620,9 +623,9 @@ __device__ __forceinline__ void cp_async16_zfill(uint32_t smem_addr, const void*
                : "memory");
 }
 
-// Grid layout of quant_qkv_kernel: a stripe of kQuantStripeCtas(per_grp) CTAs covers whole
-// token groups (lcm(per_grp, 256) threads), so a thread keeps one (head, 8-channel) lane
-// for all the token groups it visits, stepping by the grid's stripes.
+// Grid layout of quant_qkv_kernel: a stripe of CTAs covers whole tokens (lcm(per_grp, 256)
+// threads, per_grp = H * HD / 16 lanes per token), so a thread keeps one (head, 16-channel)
+// lane for all the tokens it visits, stepping by the grid's stripes.
 static inline int64_t quant_stripe_threads(int64_t per_grp) {
   int64_t a = per_grp, b = 256;
   while (b) {
@@ -633,109 +636,129 @@ static inline int64_t quant_stripe_threads(int64_t per_grp) {
   return per_grp / a * 256;   // lcm(per_grp, 256)
 }
 
-// Persistent form: each thread walks its token groups with kQuantStages groups of Q / K /
-// V rows in flight (cp.async into its own shared-memory slots; no thread reads another's),
-// and quantises one group while the next ones load.
+// (batch, token) of a row index bg = b * T + t, advanced by a fixed step without a division
+struct RowCursor {
+  int64_t b, t;
+  __device__ void advance(int64_t step, int64_t T) {
+    t += step;
+    while (t >= T) {
+      t -= T;
+      ++b;
+    }
+  }
+};
+
+// Persistent form: one thread per 16 channels of a (head, token); each thread walks its
+// tokens with kQuantStages tokens of Q / K / V rows in flight (cp.async into its own
+// shared-memory slots; no thread reads another's), and quantises one token while the next
+// ones load.
 template <int HD>
 __global__ void __launch_bounds__(256, 2) quant_qkv_kernel(QuantParams p, int stripe_ctas) {
   pdl_begin();
-  constexpr int LPH = HD / 8, TOK = kQuantTok, NS = kQuantStages, SLOTS = 3 * TOK;
-  extern __shared__ __align__(16) uint4 qbuf[];   // [NS][SLOTS][256]
+  constexpr int LPH = HD / 16, NS = kQuantStages, SLOTS = 6;   // Q, K, V x two 16-byte halves
+  extern __shared__ __align__(16) uint4 qbuf[];                // [NS][SLOTS][256]
   const int64_t per_grp = (int64_t)p.H * LPH;
-  const int64_t groups = (p.T + TOK - 1) / TOK;
-  const int64_t total_bg = (int64_t)p.B * groups;
-  const int64_t stripe_threads = (int64_t)stripe_ctas * 256;
-  const int64_t stripe_groups = stripe_threads / per_grp;
+  const int64_t total = (int64_t)p.B * p.T;
+  const int64_t stripe_rows = (int64_t)stripe_ctas * 256 / per_grp;
   const int64_t lin = (int64_t)(blockIdx.x % stripe_ctas) * 256 + threadIdx.x;
   const int hl = (int)(lin % per_grp);
-  const int h = hl / LPH, d0 = (hl % LPH) * 8;
-  const int64_t bg0 = (int64_t)(blockIdx.x / stripe_ctas) * stripe_groups;   // the CTA's first group row
-  const int64_t gi = lin / per_grp;
-  const int64_t step = (int64_t)(gridDim.x / stripe_ctas) * stripe_groups;
+  const int h = hl / LPH, d0 = (hl % LPH) * 16;
+  const int64_t row0 = (int64_t)(blockIdx.x / stripe_ctas) * stripe_rows;   // the CTA's first row
+  const int64_t step = (int64_t)(gridDim.x / stripe_ctas) * stripe_rows;
+  const int64_t first = row0 + lin / per_grp;
   const bool with_q = p.qi != nullptr, with_v = p.vi != nullptr;
   const uint32_t base = smem_u32(qbuf) + threadIdx.x * 16;
-  // loads of the k-th group this thread visits into stage k % NS (zero rows past the end)
+  const __nv_bfloat16* qh = p.q + (int64_t)h * p.sq_h + d0;
+  const __nv_bfloat16* kh = p.k + (int64_t)h * p.sk_h + d0;
+  const __nv_bfloat16* vh = p.v + (int64_t)h * p.sv_h + d0;
+  // rows visited: first + k * step for k < nk (nk uniform over the CTA, so every lane of a
+  // head takes part in every shuffle; rows past the end load zeros and store nothing)
+  const int64_t nk = row0 < total ? (total - row0 + step - 1) / step : 0;
+  RowCursor in{first / p.T, first % p.T}, out = in;
   auto issue = [&](int64_t k) {
-    const int64_t bg = bg0 + gi + k * step;
     const uint32_t sb = base + (uint32_t)((k % NS) * SLOTS * 256 * 16);
-    const int b = (int)(bg < total_bg ? bg / groups : 0);
-    const int t0 = (int)(bg < total_bg ? bg % groups : 0) * TOK;
-#pragma unroll
-    for (int i = 0; i < TOK; ++i) {
-      const bool ok = bg < total_bg && t0 + i < p.T;
-      const int64_t src_t = ok ? order_row(p.perm, t0 + i, p.T, p.err) : 0;
-      const __nv_bfloat16* q = p.q + (int64_t)b * p.sq_b + src_t * p.sq_t + (int64_t)h * p.sq_h + d0;
-      const __nv_bfloat16* k_ = p.k + (int64_t)b * p.sk_b + src_t * p.sk_t + (int64_t)h * p.sk_h + d0;
-      const __nv_bfloat16* v = p.v + (int64_t)b * p.sv_b + src_t * p.sv_t + (int64_t)h * p.sv_h + d0;
-      cp_async16_zfill(sb + (0 * TOK + i) * 256 * 16, q, ok && with_q ? 16u : 0u);
-      cp_async16_zfill(sb + (1 * TOK + i) * 256 * 16, k_, ok ? 16u : 0u);
-      cp_async16_zfill(sb + (2 * TOK + i) * 256 * 16, v, ok && with_v ? 16u : 0u);
-    }
+    const bool ok = in.b < p.B;
+    const int64_t b = ok ? in.b : 0;
+    const int64_t src_t = ok ? order_row(p.perm, in.t, p.T, p.err) : 0;   // token of row t
+    const __nv_bfloat16* q = qh + b * p.sq_b + src_t * p.sq_t;
+    const __nv_bfloat16* k_ = kh + b * p.sk_b + src_t * p.sk_t;
+    const __nv_bfloat16* v = vh + b * p.sv_b + src_t * p.sv_t;
+    const uint32_t nq = ok && with_q ? 16u : 0u, nkb = ok ? 16u : 0u, nv = ok && with_v ? 16u : 0u;
+    cp_async16_zfill(sb + 0 * 256 * 16, q, nq);
+    cp_async16_zfill(sb + 1 * 256 * 16, q + 8, nq);
+    cp_async16_zfill(sb + 2 * 256 * 16, k_, nkb);
+    cp_async16_zfill(sb + 3 * 256 * 16, k_ + 8, nkb);
+    cp_async16_zfill(sb + 4 * 256 * 16, v, nv);
+    cp_async16_zfill(sb + 5 * 256 * 16, v + 8, nv);
+    in.advance(step, p.T);
   };
-  // number of groups this CTA's threads visit (uniform over the CTA, so every lane of a
-  // head takes part in every shuffle)
-  const int64_t nk = bg0 < total_bg ? (total_bg - bg0 + step - 1) / step : 0;
 #pragma unroll
   for (int s = 0; s < NS - 1; ++s) {
     if (s < nk) issue(s);
     asm volatile("cp.async.commit_group;" ::: "memory");
   }
-  int cur_b = -1;
-  float m[8], sc[8], sc_rcp[8];
+  int64_t cur_b = -1;
+  float m[16], sc[16], sc_rcp[16];
   for (int64_t k = 0; k < nk; ++k) {
     if (k + NS - 1 < nk) issue(k + NS - 1);
     asm volatile("cp.async.commit_group;" ::: "memory");
     asm volatile("cp.async.wait_group %0;" ::"n"(NS - 1) : "memory");
-    const int64_t bg = bg0 + gi + k * step;
-    const bool live = bg < total_bg;
-    const int b = (int)(live ? bg / groups : 0);
-    const int t0 = (int)(live ? bg % groups : 0) * TOK;
+    const bool ok = out.b < p.B;
+    const int64_t b = ok ? out.b : 0, t = out.t;
+    out.advance(step, p.T);
     if (b != cur_b) {   // per-(b, h) constants of this lane
       cur_b = b;
-      const float4* mp = reinterpret_cast<const float4*>(p.kmean + ((int64_t)b * p.H + h) * HD + d0);
-      const float4 m0 = __ldg(mp), m1 = __ldg(mp + 1);
-      m[0] = m0.x; m[1] = m0.y; m[2] = m0.z; m[3] = m0.w; m[4] = m1.x; m[5] = m1.y; m[6] = m1.z; m[7] = m1.w;
+      const float4* mp = reinterpret_cast<const float4*>(p.kmean + (b * p.H + h) * HD + d0);
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const float4 mj = __ldg(mp + j);
+        m[4 * j] = mj.x; m[4 * j + 1] = mj.y; m[4 * j + 2] = mj.z; m[4 * j + 3] = mj.w;
+      }
       if (with_v) {
-        const float4* sp = reinterpret_cast<const float4*>(p.vscale + ((int64_t)b * p.H + h) * HD + d0);
-        const float4 s0 = __ldg(sp), s1 = __ldg(sp + 1);
-        sc[0] = s0.x; sc[1] = s0.y; sc[2] = s0.z; sc[3] = s0.w; sc[4] = s1.x; sc[5] = s1.y; sc[6] = s1.z; sc[7] = s1.w;
+        const float4* sp = reinterpret_cast<const float4*>(p.vscale + (b * p.H + h) * HD + d0);
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const float4 sj = __ldg(sp + j);
+          sc[4 * j] = sj.x; sc[4 * j + 1] = sj.y; sc[4 * j + 2] = sj.z; sc[4 * j + 3] = sj.w;
+        }
       }
 #pragma unroll
-      for (int c = 0; c < 8; ++c) sc_rcp[c] = with_v ? __frcp_rn(sc[c]) : 0.f;
+      for (int c = 0; c < 16; ++c) sc_rcp[c] = with_v ? __frcp_rn(sc[c]) : 0.f;
     }
     const uint4* sl = qbuf + (k % NS) * SLOTS * 256 + threadIdx.x;
+    const int64_t o = ((b * p.T + t) * p.H + h) * HD + d0;
+    const int64_t so = (b * p.H + h) * p.tp + t;
+    float x[16];
+    if (with_q) {
+      float s;
+      unpack8(sl[0], *reinterpret_cast<float(*)[8]>(&x[0]));
+      unpack8(sl[256], *reinterpret_cast<float(*)[8]>(&x[8]));
+      const uint4 cq = token_codes<LPH>(x, s);
+      if (ok) {
+        *reinterpret_cast<uint4*>(p.qi + o) = cq;
+        if (d0 == 0) p.qs[so] = s;
+      }
+    }
+    {
+      float s;
+      unpack8(sl[2 * 256], *reinterpret_cast<float(*)[8]>(&x[0]));
+      unpack8(sl[3 * 256], *reinterpret_cast<float(*)[8]>(&x[8]));
 #pragma unroll
-    for (int i = 0; i < TOK; ++i) {
-      const int t = t0 + i;
-      const bool ok = live && t < p.T;
-      const int64_t o = (((int64_t)b * p.T + t) * p.H + h) * HD + d0;
-      const int64_t so = ((int64_t)b * p.H + h) * p.tp + t;
-      if (with_q) {
-        float xq[8], s;
-        unpack8(sl[(0 * TOK + i) * 256], xq);
-        const uint2 cq = token_codes<LPH>(xq, s);
-        if (ok) {
-          *reinterpret_cast<uint2*>(p.qi + o) = cq;
-          if (d0 == 0) p.qs[so] = s;
-        }
+      for (int c = 0; c < 16; ++c) x[c] = __fsub_rn(x[c], m[c]);
+      const uint4 ck = token_codes<LPH>(x, s);
+      if (ok) {
+        *reinterpret_cast<uint4*>(p.ki + o) = ck;
+        if (d0 == 0) p.ks[so] = s;
       }
-      {
-        float xk[8], s;
-        unpack8(sl[(1 * TOK + i) * 256], xk);
-#pragma unroll
-        for (int c = 0; c < 8; ++c) xk[c] = __fsub_rn(xk[c], m[c]);
-        const uint2 ck = token_codes<LPH>(xk, s);
-        if (ok) {
-          *reinterpret_cast<uint2*>(p.ki + o) = ck;
-          if (d0 == 0) p.ks[so] = s;
-        }
-      }
-      if (with_v) {
-        float xv[8];
-        unpack8(sl[(2 * TOK + i) * 256], xv);
-        const uint2 cv = quant8(xv, sc, sc_rcp);
-        if (ok) *reinterpret_cast<uint2*>(p.vi + o) = cv;
-      }
+    }
+    if (with_v) {
+      unpack8(sl[4 * 256], *reinterpret_cast<float(*)[8]>(&x[0]));
+      unpack8(sl[5 * 256], *reinterpret_cast<float(*)[8]>(&x[8]));
+      const uint2 a = quant8(*reinterpret_cast<const float(*)[8]>(&x[0]), *reinterpret_cast<const float(*)[8]>(&sc[0]),
+                             *reinterpret_cast<const float(*)[8]>(&sc_rcp[0]));
+      const uint2 c2 = quant8(*reinterpret_cast<const float(*)[8]>(&x[8]), *reinterpret_cast<const float(*)[8]>(&sc[8]),
+                              *reinterpret_cast<const float(*)[8]>(&sc_rcp[8]));
+      if (ok) *reinterpret_cast<uint4*>(p.vi + o) = make_uint4(a.x, a.y, c2.x, c2.y);
     }
   }
   asm volatile("cp.async.wait_all;" ::: "memory");
@@ -984,14 +1007,14 @@ void launch_quant_qkv(const QuantParams& p, int hd, cudaStream_t st) {
     cudaGetDevice(&dev);
     sms = cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) == cudaSuccess && n > 0 ? n : 148;
   }
-  const int64_t per_grp = (int64_t)p.H * (hd / 8);
-  const int stripe_ctas = (int)(quant_stripe_threads(per_grp) / 256);
-  const int64_t total_bg = (int64_t)p.B * ((p.T + kQuantTok - 1) / kQuantTok);
-  const int64_t stripe_groups = quant_stripe_threads(per_grp) / per_grp;
+  const int64_t per_grp = (int64_t)p.H * (hd / 16);
+  const int64_t stripe_threads = quant_stripe_threads(per_grp);
+  const int stripe_ctas = (int)(stripe_threads / 256);
+  const int64_t total = (int64_t)p.B * p.T, stripe_rows = stripe_threads / per_grp;
   int64_t stripes = std::max<int64_t>(1, (2 * (int64_t)sms) / stripe_ctas);   // two CTAs per SM
-  stripes = std::min<int64_t>(stripes, (total_bg + stripe_groups - 1) / stripe_groups);
+  stripes = std::min<int64_t>(stripes, (total + stripe_rows - 1) / stripe_rows);
   const dim3 grid((unsigned)(stripes * stripe_ctas));
-  const size_t smem = (size_t)kQuantStages * 3 * kQuantTok * 256 * 16;
+  const size_t smem = (size_t)kQuantStages * 6 * 256 * 16;
   if (hd == 128) {
     cudaFuncSetAttribute(quant_qkv_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     launch_pdl(quant_qkv_kernel<128>, grid, dim3(256), smem, st, p, stripe_ctas);
