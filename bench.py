@@ -522,6 +522,27 @@ def _sampler_units(units):
     return time.perf_counter() - t0, prep_s, len(units)
 
 
+def cpu_sdpa_dense(rows=2048):
+    """torch CPU SDPA (dense, fp32: the CPU path's dense attention) on head 0 of config 3:
+    `rows` query rows against all 32760 keys, timed once after a warm-up on a smaller
+    slice, extrapolated to the call's 40 heads x 32760 rows. Uses torch's intra-op
+    threads."""
+    import torch
+    from solb200.workloads import CONFIGS, make_qkv
+    cfg = CONFIGS["c3"]
+    q, k, v = (t.float().transpose(1, 2) for t in make_qkv(cfg, heads=slice(0, 1)))   # [1, 1, T, D]
+    sdpa = torch.nn.functional.scaled_dot_product_attention
+    sdpa(q[:, :, :256], k, v)
+    t0 = time.perf_counter()
+    sdpa(q[:, :, :rows], k, v)
+    sec = time.perf_counter() - t0
+    ms = sec * 1e3 * (cfg.tokens / rows) * cfg.heads * cfg.batch
+    return {"ms_per_call": ms, "value": cfg.dense_flops() / (ms * 1e-3) / 1e12, "unit": UNIT,
+            "cores": torch.get_num_threads(),
+            "sample": f"{rows} query rows of head 0 x {cfg.tokens} keys, fp32, extrapolated to "
+                      f"{cfg.heads} heads x {cfg.tokens} rows"}
+
+
 class CpuSampler:
     """The oracle port (the reference's algorithm restated on the CPU, pinned to the
     reference's own kernels) on `procs` spawned host processes, one thread each, over head
@@ -733,6 +754,10 @@ def main():
             result["cpu_baseline"] = {
                 "value": CONFIGS["c3"].dense_flops() / (ms_cpu * 1e-3) / 1e12, "unit": UNIT,
                 "cores": 1, "kind": "port", "sample": sampler.info(args.cpu_units), "ms_per_call": ms_cpu}
+            try:
+                result["cpu_baseline"]["dense_sdpa_cpu"] = cpu_sdpa_dense()
+            except Exception as exc:   # pragma: no cover
+                result["cpu_baseline"]["dense_sdpa_cpu"] = {"error": str(exc)[:200]}
         except Exception as exc:   # pragma: no cover
             result["cpu_baseline"] = {"error": str(exc)}
     emit(result)
