@@ -348,6 +348,18 @@ __device__ __forceinline__ void named_bar_sync(int id, int count) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(count) : "memory");
 }
 
+// Per-warpgroup register budgets (executed by all four warps of a warpgroup together).
+// The increases draw on what the decreases release: the block's launch total (threads x
+// registers per thread at launch) must cover the sum of the new budgets.
+template <int N>
+__device__ __forceinline__ void regs_increase() {
+  asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(N));
+}
+template <int N>
+__device__ __forceinline__ void regs_decrease() {
+  asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(N));
+}
+
 // Packed fp32 pairs (Blackwell f32x2 FMA / add): one instruction for two lanes' worth
 // of arithmetic.
 __device__ __forceinline__ float2 fma2(float2 a, float2 b, float2 c) {

@@ -23,10 +23,11 @@
 // the epilogue multiplies by vscale[d] (an approximate-tile contribution made before the
 // first fold is divided by vscale[d] once).
 //
-// One CTA per unit, 192 threads: warps 0-3 softmax + fold + epilogue (thread = query row
-// = TMEM lane), warp 4 TMA producer, warp 5 TMEM allocator + MMA issuer. Two CTAs share
-// an SM (256 TMEM columns and ~99 KB of shared memory each), so one CTA's tensor-core
-// phases overlap the other's softmax.
+// One CTA per unit, 256 threads: warps 0-3 softmax + fold + epilogue (thread = query row
+// = TMEM lane), warp 4 TMA producer, warp 5 TMEM allocator + MMA issuer, warps 6-7 idle
+// (they complete the second warpgroup, whose registers the softmax warps take). Two CTAs
+// share an SM (256 TMEM columns and ~99 KB of shared memory each), so one CTA's
+// tensor-core phases overlap the other's softmax.
 //   TMEM   [0, 128)  S: scores (fp32 or int32), then bf16 P or the int32 P.V
 //          [128, 128 + HD)  O (fp32)
 //   smem   region Q (32 KB): bf16 q for the approximate tiles; then qi at +0 and the int8
@@ -198,7 +199,7 @@ __device__ __forceinline__ void to_vscale_units(uint32_t t_o, const float* __res
 }  // namespace
 
 template <int HD, int BLK>
-__global__ void __launch_bounds__(192, 2)
+__global__ void __launch_bounds__(256, 2)
 sol_fwd_int8_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_kc,
                     const __grid_constant__ CUtensorMap tm_vc, const __grid_constant__ CUtensorMap tm_o,
                     const __grid_constant__ CUtensorMap tm_qi, const __grid_constant__ CUtensorMap tm_ki,
@@ -282,6 +283,10 @@ sol_fwd_int8_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_const
   // e % 2 with int8 P.V (int8 vi tiles) or stage 0 with bf16 P.V (one bf16 V tile).
   auto vstage = [&](bool exact, int e) { return exact && pv8 ? (e & 1) : 0; };
 
+  // Launched at 128 registers a thread: the producer / MMA warpgroup (warps 4-7, two of
+  // them idle) keeps 40, the softmax warpgroup takes 216 (128 x 40 + 128 x 216 = 256 x 128;
+  // measured best of 24-56 for the producer side: the softmax path spills at 168).
+  if (warp >= 4) regs_decrease<40>();
   if (warp == 4) {
     // ------------------------------------------------------------ TMA producer
     if (lane == 0) {
@@ -414,8 +419,9 @@ sol_fwd_int8_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_const
       tc_commit(bar_drain);
       mbar_wait(bar_drain, 0, p.err, kErrWaitDrain);
     }
-  } else {
+  } else if (warp < 4) {
     // ------------------------------------------- softmax, fold and epilogue (rows)
+    regs_increase<216>();
     const int row = threadIdx.x;
     const uint32_t lane_base = (uint32_t)(warp * 32) << 16;
     if (p.perm) prefetch_row_token<BLK>(p, u, row, sTok);
@@ -562,7 +568,7 @@ static cudaError_t launch_t(const FwdMaps& m, const FwdParams& p, cudaStream_t s
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return e;
   const unsigned grid = (unsigned)((int64_t)p.B * p.H * p.N);
-  return launch_pdl(kern, dim3(grid), dim3(192), smem, st, m.q, m.kc, m.vc, m.o, m.qi, m.ki, m.vi, m.v, p);
+  return launch_pdl(kern, dim3(grid), dim3(256), smem, st, m.q, m.kc, m.vc, m.o, m.qi, m.ki, m.vi, m.v, p);
 }
 
 cudaError_t launch_fwd_int8(int hd, int blk, const FwdMaps& m, const FwdParams& p, cudaStream_t st) {
