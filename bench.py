@@ -176,6 +176,28 @@ def executed_flops(torch, ws, B, H, T, D, blk):
 
 # ------------------------------------------------------------------ our arm
 
+def bind_gpu_local_cpus(torch, local_rank):
+    """Run this process on the CPUs local to its GPU, so that the pinned host buffers of the
+    e2e leg (placed on first touch) sit on the GPU's NUMA node. Returns the CPU list it
+    bound to, or None when the PCI topology is not readable or shares no CPU with the
+    allowed set."""
+    try:
+        p = torch.cuda.get_device_properties(local_rank)
+        bus = f"{p.pci_domain_id:04x}:{p.pci_bus_id:02x}:{p.pci_device_id:02x}.0"
+        text = open(f"/sys/bus/pci/devices/{bus}/local_cpulist").read().strip()
+        cpus = set()
+        for part in text.split(","):
+            lo, _, hi = part.partition("-")
+            cpus.update(range(int(lo), int(hi or lo) + 1))
+        cpus &= os.sched_getaffinity(0)
+        if not cpus:
+            return None
+        os.sched_setaffinity(0, cpus)
+        return text
+    except Exception:
+        return None
+
+
 class Ctx:
     """What every measurement of our arm needs."""
 
@@ -187,6 +209,7 @@ class Ctx:
         self.args, self.rank, self.world, self.local_rank = args, rank, world, local_rank
         self.dev = torch.device("cuda", local_rank)
         torch.cuda.set_device(self.dev)
+        self.host_cpus = bind_gpu_local_cpus(torch, local_rank)
         self.lib = _lib.lib()
         self.timer = Timer(torch, dist, self.dev, world)
 
@@ -285,6 +308,7 @@ def e2e_block(ctx, q, k, v, cfg, path):
     return {"value": cfg.dense_flops() / (ms * 1e-3) / 1e12, "unit": UNIT, "ms_per_step": ms,
             "h2d_bytes_per_step": h2d * ctx.world, "d2h_bytes_per_step": d2h * ctx.world,
             "h2d_gbs_per_rank": h2d / (ms * 1e-3) / 1e9,
+            "host_cpus": ctx.host_cpus or "unbound",
             "api": "solb200.sol_attn_host (pinned host in and out, head chunks streamed)"}
 
 
@@ -736,11 +760,13 @@ def main():
         from datetime import timedelta
         dist.init_process_group("nccl", timeout=timedelta(seconds=120),
                                 device_id=torch.device("cuda", local_rank))
+    all_cpus = os.sched_getaffinity(0)
     try:
         result = run_ours(args, rank, world, local_rank)
     finally:
         if world > 1:
             dist.destroy_process_group()
+        os.sched_setaffinity(0, all_cpus)   # the CPU legs below use every allowed core
     if rank != 0:
         return
     if not args.no_cpu_baseline and world == 1:
