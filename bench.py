@@ -651,6 +651,10 @@ def reference_arm(args, world):
         sampler.close()
     ms = statistics.median(times)
     val = cfg.dense_flops() / (ms * 1e-3) / 1e12
+    try:   # the dense half of the reference's CPU path: torch CPU SDPA
+        dense_cpu = cpu_sdpa_dense()
+    except Exception as exc:   # pragma: no cover
+        dense_cpu = {"error": str(exc)[:200]}
     emit({
         "impl": "reference", "metric": METRIC, "value": val, "unit": UNIT, "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
@@ -658,7 +662,7 @@ def reference_arm(args, world):
         "data": "synthetic (seeded smooth+noise video-DiT q/k/v, solb200.workloads)",
         "config": bench_config(args.path, world),
         "cpu_baseline": {"value": val, "unit": UNIT, "cores": procs, "kind": "port",
-                         "sample": sampler.info(args.ref_units)},
+                         "sample": sampler.info(args.ref_units), "dense_sdpa_cpu": dense_cpu},
         "e2e": {"value": val, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     })
 
