@@ -149,6 +149,23 @@ def test_fused_preprocess_bitexact(cuda_device, name, int8_pv):
         assert_bitexact(got[6], g["i8_ks"][:, :T], "ks vs reference")
 
 
+@pytest.mark.parametrize("B,T,H,D", [(2, 1000, 5, 128), (1, 777, 3, 64), (3, 300, 7, 128)])
+def test_quantiser_layouts_bitexact(cuda_device, B, T, H, D):
+    """The Q/K/V quantiser's persistent stripes for head counts whose lanes do not fill a
+    warp per token (warps spanning two tokens), batches > 1 (the row cursor crossing a
+    batch) and ragged token counts: every code and scale equals the oracle's."""
+    gen = torch.Generator().manual_seed(B * 1000 + T + H)
+    q, k, v = ((torch.randn(B, T, H, D, generator=gen) * s).to(torch.bfloat16) for s in (1.0, 0.7, 1.3))
+    blk = 64
+    got = solb200.fused_preprocess(q.cuda(), k.cuda(), v.cuda(), tau=0.9, scale=D ** -0.5, int8_pv=True, block=blk)
+    want = O.fused_preprocess(*(O.to_np(t) for t in (q, k, v)), 0.9, D ** -0.5, T, blk, int8_pv=True)
+    for nm, val in zip(["kc", "vc", "thr", "qi", "qs", "ki", "ks", "vi", "vsc"], got):
+        w = want[nm]
+        if nm == "vsc":
+            w = w.reshape(-1, D)
+        assert_bitexact(val, w, f"{nm} B={B} T={T} H={H} D={D}")
+
+
 @pytest.mark.parametrize("name", CASES)
 @pytest.mark.parametrize("int8", [False, True])
 def test_routing_mask_parity(cuda_device, name, int8):
