@@ -255,6 +255,15 @@ def measure_c3(ctx, path, q, k, v, cfg):
     for _ in range(2):
         call(STAGES_FORWARD)
     ms_fwd = ctx.timer(lambda: call(STAGES_FORWARD), steps)
+    # PREPARE in its parts (each timed alone, so each carries its own launch latency)
+    from solb200._lib import STAGES_POOL, STAGES_QUANT, STAGES_ROUTE
+    parts = {"pool": STAGES_POOL, "route": STAGES_ROUTE}
+    if path == "int8":
+        parts["quant"] = STAGES_QUANT
+    ms_parts = {}
+    for name, st in parts.items():
+        call(st)
+        ms_parts[name] = ctx.timer(lambda st=st: call(st), steps)
     ws.check_device_error()
     flops, density = executed_flops(torch, ws, B, H, T, D, cfg.block)
     # the slowest rank's forward decides the job; flops summed over ranks
@@ -263,7 +272,7 @@ def measure_c3(ctx, path, q, k, v, cfg):
         t = torch.tensor([flops], device=ctx.dev, dtype=torch.float64)
         ctx.dist.all_reduce(t)
         flops_all = float(t.item())
-    return dict(ms=ms, ms_prep=ms_prep, ms_fwd=ms_fwd, flops=flops, flops_all=flops_all,
+    return dict(ms=ms, ms_prep=ms_prep, ms_fwd=ms_fwd, ms_parts=ms_parts, flops=flops, flops_all=flops_all,
                 density=density, clocks=clk.result, ws=ws, out=out)
 
 
@@ -273,7 +282,7 @@ def int8_block(ctx, m, cfg, peaks):
     achieved = m["flops_all"] / ctx.world / (m["ms_fwd"] * 1e-3) / 1e12   # one GPU's launch
     return {
         "ms_per_call": m["ms"], "value": cfg.dense_flops() / (m["ms"] * 1e-3) / 1e12, "unit": UNIT,
-        "stages_ms": {"prep_route": m["ms_prep"], "forward": m["ms_fwd"]},
+        "stages_ms": {"prep_route": m["ms_prep"], **m["ms_parts"], "forward": m["ms_fwd"]},
         "routed_density": m["density"],
         "roofline": {"bound": "tensor", "kernel": "sol_fwd_int8_kernel", "achieved": achieved,
                      "unit": "TOP/s", "peak_bf16": peaks["bf16"], "frac_of_bf16_peak": achieved / peaks["bf16"],
@@ -500,7 +509,8 @@ def run_ours(args, rank, world, local_rank):
         "data": "synthetic (seeded smooth+noise video-DiT q/k/v, solb200.workloads)",
         "config": config,
         "routed_density": m["density"],
-        "stages_ms": {"prep_route": m["ms_prep"], "forward": m["ms_fwd"], "reorder_qkv_and_o": ms_reorder},
+        "stages_ms": {"prep_route": m["ms_prep"], **m["ms_parts"], "forward": m["ms_fwd"],
+                      "reorder_qkv_and_o": ms_reorder},
         "dense_sdpa_ms": ms_dense,
         "sparse_over_dense": (ms / ms_dense) if ms_dense else None,
         "roofline": {"bound": "tensor", "kernel": f"sol_fwd_{args.path}_kernel",

@@ -204,10 +204,14 @@ int32_t run(const Plan& P, const Call& c) {
   if ((rc = check_tensor("q", c.q, c.sq, P.B))) return rc;
   if ((rc = check_tensor("k", c.k, c.sk, P.B))) return rc;
   if ((rc = check_tensor("v", c.v, c.sv, P.B))) return rc;
-  if (c.stages != SOLB200_STAGES_ALL && c.stages != SOLB200_STAGES_PREPARE && c.stages != SOLB200_STAGES_FORWARD)
+  if (c.stages < SOLB200_STAGES_ALL || c.stages > SOLB200_STAGES_ROUTE)
     return fail(SOLB200_ERR_INVALID, "unknown stages value");
-  const bool prep = c.stages != SOLB200_STAGES_FORWARD;
-  if (c.stages != SOLB200_STAGES_PREPARE && (!c.out || !aligned16(c.out)))
+  const bool whole_prep = c.stages == SOLB200_STAGES_ALL || c.stages == SOLB200_STAGES_PREPARE;
+  const bool do_pool = whole_prep || c.stages == SOLB200_STAGES_POOL;
+  const bool do_quant = whole_prep || c.stages == SOLB200_STAGES_QUANT;
+  const bool do_route = whole_prep || c.stages == SOLB200_STAGES_ROUTE;
+  const bool do_fwd = c.stages == SOLB200_STAGES_ALL || c.stages == SOLB200_STAGES_FORWARD;
+  if (do_fwd && (!c.out || !aligned16(c.out)))
     return fail(SOLB200_ERR_ALIGNMENT, "out: null or not 16-byte aligned");
   if (!c.ws || c.ws_bytes < P.total)
     return fail(SOLB200_ERR_WORKSPACE, "workspace is " + std::to_string(c.ws_bytes) + " bytes, needs " +
@@ -241,7 +245,7 @@ int32_t run(const Plan& P, const Call& c) {
       copies[i] = reinterpret_cast<__nv_bfloat16*>(static_cast<char*>(c.ws) + P.off_copy[i]);
   pp.qcopy = copies[0]; pp.kcopy = copies[1]; pp.vcopy = copies[2];
   pp.B = (int)P.B; pp.T = (int)P.T; pp.H = (int)P.H; pp.N = P.N; pp.npad = P.npad; pp.blk = P.blk;
-  if (prep) launch_pool(pp, hd, pp.vamax != nullptr, c.st);
+  if (do_pool) launch_pool(pp, hd, pp.vamax != nullptr, c.st);
 
   MomentsParams mp{};
   mp.kc = pp.kc;
@@ -250,9 +254,9 @@ int32_t run(const Plan& P, const Call& c) {
   mp.kvar = at<float>(c.ws, P, SOLB200_BUF_KVAR);
   mp.vscale = c.int8 ? at<float>(c.ws, P, SOLB200_BUF_VSCALE) : nullptr;
   mp.B = (int)P.B; mp.H = (int)P.H; mp.N = P.N; mp.npad = P.npad;
-  if (prep) launch_moments(mp, hd, c.int8, c.st);
+  if (do_pool) launch_moments(mp, hd, c.int8, c.st);
 
-  if (c.int8 && prep) {
+  if (c.int8 && do_quant) {
     QuantParams qp{};
     qp.q = pp.q; qp.k = pp.k; qp.v = pp.v;
     qp.sq_b = pp.sq_b; qp.sq_t = pp.sq_t; qp.sq_h = pp.sq_h;
@@ -287,13 +291,13 @@ int32_t run(const Plan& P, const Call& c) {
   auto clampi = [&](int64_t x) { return (int)(x < -lim ? -lim : (x > lim ? lim : x)); };
   rp.sink_kv0 = clampi(c.sink_kv[0]); rp.sink_kv1 = clampi(c.sink_kv[1]);
   rp.sink_q0 = clampi(c.sink_q[0]); rp.sink_q1 = clampi(c.sink_q[1]);
-  if (prep) {
+  if (do_route) {
     launch_route(rp, hd, c.st);
     launch_order(rp.count, at<int>(c.ws, P, SOLB200_BUF_ORDER), (int)(P.B * P.H), P.N, c.st);
   }
   e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, "preprocess launch");
-  if (c.stages == SOLB200_STAGES_PREPARE) return SOLB200_OK;
+  if (!do_fwd) return SOLB200_OK;
 
   FwdParams fp{};
   fp.mask = rp.mask;

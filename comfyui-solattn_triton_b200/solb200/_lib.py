@@ -23,6 +23,7 @@ STATUS = {
 BUF = dict(error=0, kc=1, vc=2, centroid=3, kmean=4, kvar=5, thr=6, mask=7, count=8, vamax=9,
            vscale=10, qi=11, qs=12, ki=13, ks=14, vi=15, order=16)
 STAGES_ALL, STAGES_PREPARE, STAGES_FORWARD = 0, 1, 2
+STAGES_POOL, STAGES_QUANT, STAGES_ROUTE = 3, 4, 5   # PREPARE in parts (per-stage timing)
 
 _lib = None
 

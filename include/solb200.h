@@ -55,8 +55,15 @@ enum solb200_status {
 enum solb200_stages {
   SOLB200_STAGES_ALL = 0,     /* preprocess, route, forward */
   SOLB200_STAGES_PREPARE = 1, /* preprocess and route only (no output written) */
-  SOLB200_STAGES_FORWARD = 2  /* forward only, over a workspace that an earlier ALL or PREPARE
+  SOLB200_STAGES_FORWARD = 2, /* forward only, over a workspace that an earlier ALL or PREPARE
                                  call with the same inputs and geometry filled (profiling) */
+  /* PREPARE in parts, for per-stage timing: run in this order on one workspace, they leave
+     it as one PREPARE call does (profiling) */
+  SOLB200_STAGES_POOL = 3,    /* K / V / Q pooling and the kc moments (INT8: k_mean, centred kc,
+                                 V scales) */
+  SOLB200_STAGES_QUANT = 4,   /* INT8 only: the Q / K / V codes and scales, after POOL */
+  SOLB200_STAGES_ROUTE = 5    /* routing (thresholds, mask, counts) and the forward's schedule,
+                                 after POOL */
 };
 
 /* Workspace intermediates whose byte offsets solb200_workspace_offset() reports. */

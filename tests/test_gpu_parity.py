@@ -379,3 +379,36 @@ def test_forward_schedule(cuda_device):
         c = counts[seg]
         assert (np.diff(c) <= 0).all(), "query blocks not by descending count"
     assert counts.min() < counts.max(), "fixture should have uneven counts"
+
+
+@pytest.mark.parametrize("int8", [False, True])
+def test_stage_parts_equal_one_call(cuda_device, int8):
+    """POOL, QUANT (INT8), ROUTE and FORWARD run as separate C-ABI calls on one workspace
+    produce the one-call output bit for bit (the per-stage timing of the bench uses them)."""
+    from solb200._lib import (STAGES_ALL, STAGES_FORWARD, STAGES_POOL, STAGES_QUANT, STAGES_ROUTE, I64x2, I64x3,
+                              check, lib)
+    from solb200.ops import Workspace
+    g = torch.Generator().manual_seed(21)
+    B, T, H, D, blk = 1, 3000, 3, 128, 128
+    q, k, v = (torch.randn(B, T, H, D, generator=g).to(torch.bfloat16).cuda() for _ in range(3))
+    st = torch.cuda.current_stream().cuda_stream
+
+    def run(stages_list):
+        ws = Workspace(B, T, H, D, blk, int8, q.device)
+        out = torch.zeros_like(q)
+        for stages in stages_list:
+            a = [q.data_ptr(), I64x3(*q.stride()[:3]), k.data_ptr(), I64x3(*k.stride()[:3]), v.data_ptr(),
+                 I64x3(*v.stride()[:3]), out.data_ptr(), B, T, H, D, blk, D ** -0.5, 0.9, I64x2(0, 0), I64x2(0, 0)]
+            tail = [stages, ws.ptr(), ws.nbytes, None, None, st]
+            rc = lib().solb200_sol_attn_int8(*a, 1, *tail) if int8 else lib().solb200_sol_attn_bf16(*a, *tail)
+            check(rc, f"stages {stages}")
+        ws.check_device_error()
+        return out
+
+    whole = run([STAGES_ALL])
+    parts = run([STAGES_POOL] + ([STAGES_QUANT] if int8 else []) + [STAGES_ROUTE, STAGES_FORWARD])
+    assert torch.equal(whole, parts)
+    ws = Workspace(B, T, H, D, blk, int8, q.device)
+    a = [q.data_ptr(), I64x3(*q.stride()[:3]), k.data_ptr(), I64x3(*k.stride()[:3]), v.data_ptr(),
+         I64x3(*v.stride()[:3]), whole.data_ptr(), B, T, H, D, blk, D ** -0.5, 0.9, I64x2(0, 0), I64x2(0, 0)]
+    assert lib().solb200_sol_attn_bf16(*a, 6, ws.ptr(), ws.nbytes, None, None, st) == 1   # unknown stage: invalid
