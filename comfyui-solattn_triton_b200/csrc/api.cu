@@ -4,6 +4,8 @@
 #include <mutex>
 #include <string>
 
+#include <nvtx3/nvToolsExt.h>
+
 #include "fwd_common.cuh"
 #include "internal.h"
 #include "prep.cuh"
@@ -12,6 +14,15 @@
 using namespace solb200;
 
 namespace {
+
+// Host-side NVTX range: a named interval on the launching thread under which profilers
+// group the kernels launched inside it (a few ns when no profiler is attached).
+struct NvtxRange {
+  explicit NvtxRange(const char* name) { nvtxRangePushA(name); }
+  ~NvtxRange() { nvtxRangePop(); }
+  NvtxRange(const NvtxRange&) = delete;
+  NvtxRange& operator=(const NvtxRange&) = delete;
+};
 
 thread_local std::string g_last_error;
 
@@ -245,7 +256,10 @@ int32_t run(const Plan& P, const Call& c) {
       copies[i] = reinterpret_cast<__nv_bfloat16*>(static_cast<char*>(c.ws) + P.off_copy[i]);
   pp.qcopy = copies[0]; pp.kcopy = copies[1]; pp.vcopy = copies[2];
   pp.B = (int)P.B; pp.T = (int)P.T; pp.H = (int)P.H; pp.N = P.N; pp.npad = P.npad; pp.blk = P.blk;
-  if (do_pool) launch_pool(pp, hd, pp.vamax != nullptr, c.st);
+  if (do_pool) {
+    NvtxRange r("solb200.pool");
+    launch_pool(pp, hd, pp.vamax != nullptr, c.st);
+  }
 
   MomentsParams mp{};
   mp.kc = pp.kc;
@@ -254,9 +268,13 @@ int32_t run(const Plan& P, const Call& c) {
   mp.kvar = at<float>(c.ws, P, SOLB200_BUF_KVAR);
   mp.vscale = c.int8 ? at<float>(c.ws, P, SOLB200_BUF_VSCALE) : nullptr;
   mp.B = (int)P.B; mp.H = (int)P.H; mp.N = P.N; mp.npad = P.npad;
-  if (do_pool) launch_moments(mp, hd, c.int8, c.st);
+  if (do_pool) {
+    NvtxRange r("solb200.moments");
+    launch_moments(mp, hd, c.int8, c.st);
+  }
 
   if (c.int8 && do_quant) {
+    NvtxRange r("solb200.quant");
     QuantParams qp{};
     qp.q = pp.q; qp.k = pp.k; qp.v = pp.v;
     qp.sq_b = pp.sq_b; qp.sq_t = pp.sq_t; qp.sq_h = pp.sq_h;
@@ -292,6 +310,7 @@ int32_t run(const Plan& P, const Call& c) {
   rp.sink_kv0 = clampi(c.sink_kv[0]); rp.sink_kv1 = clampi(c.sink_kv[1]);
   rp.sink_q0 = clampi(c.sink_q[0]); rp.sink_q1 = clampi(c.sink_q[1]);
   if (do_route) {
+    NvtxRange r("solb200.route");
     launch_route(rp, hd, c.st);
     launch_order(rp.count, at<int>(c.ws, P, SOLB200_BUF_ORDER), (int)(P.B * P.H), P.N, c.st);
   }
@@ -336,6 +355,7 @@ int32_t run(const Plan& P, const Call& c) {
   if (!c.int8) {
     if ((rc = make_map(&m.k, ksrc, false, P.D, P.H, P.T, P.B, skm[2], skm[1], skm[0], kv_rows, "k"))) return rc;
     if ((rc = make_map(&m.v, vsrc, false, P.D, P.H, P.T, P.B, svm[2], svm[1], svm[0], kv_rows, "v"))) return rc;
+    NvtxRange r("solb200.forward");
     e = launch_fwd_bf16(hd, P.blk, m, fp, c.st);
     if (e != cudaSuccess) return cuda_fail(e, "bf16 forward launch");
     return SOLB200_OK;
@@ -356,7 +376,10 @@ int32_t run(const Plan& P, const Call& c) {
   fp.ks = at<float>(c.ws, P, SOLB200_BUF_KS);
   fp.vscale = mp.vscale;
   fp.int8_pv = c.int8_pv ? 1 : 0;
-  e = launch_fwd_int8(hd, P.blk, m, fp, c.st);
+  {
+    NvtxRange r("solb200.forward_int8");
+    e = launch_fwd_int8(hd, P.blk, m, fp, c.st);
+  }
   if (e != cudaSuccess) return cuda_fail(e, "int8 forward launch");
   return SOLB200_OK;
 }
@@ -502,7 +525,10 @@ int32_t solb200_attn_dense(const void* q, const int64_t* q_strides, const void* 
   if ((rc = make_map(&m.o, out, false, D, H, q_tokens, batch, D, H * D, q_tokens * H * D, BLK, "out"))) return rc;
   m.kc = m.k;   // no pooled keys / values in a dense call: valid maps that are never loaded
   m.vc = m.v;
-  e = launch_fwd_bf16((int)head_dim, BLK, m, fp, st);
+  {
+    NvtxRange r("solb200.dense");
+    e = launch_fwd_bf16((int)head_dim, BLK, m, fp, st);
+  }
   if (e != cudaSuccess) return cuda_fail(e, "dense forward launch");
   return SOLB200_OK;
 }
