@@ -564,6 +564,16 @@ static size_t fwd_int8_smem_bytes(int blk) { return (size_t)3 * 32768 + 4 * blk 
 template <int HD, int BLK>
 static cudaError_t launch_t(const FwdMaps& m, const FwdParams& p, cudaStream_t st) {
   auto kern = sol_fwd_int8_kernel<HD, BLK>;
+  // the register split (40 + 216) adds up to the launch total only at 128 registers a
+  // thread: with fewer, the softmax warpgroup's increase could never be granted
+  static int launch_regs = 0;
+  if (launch_regs == 0) {
+    cudaFuncAttributes fa{};
+    cudaError_t ea = cudaFuncGetAttributes(&fa, kern);
+    if (ea != cudaSuccess) return ea;
+    launch_regs = fa.numRegs;
+  }
+  if (launch_regs != 128) return cudaErrorInvalidConfiguration;
   const size_t smem = fwd_int8_smem_bytes(BLK);
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return e;
