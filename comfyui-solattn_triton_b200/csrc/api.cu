@@ -477,10 +477,11 @@ int32_t solb200_sol_attn_reordered(const void* q, const int64_t* q_strides, cons
                     workspace_bytes, nullptr, nullptr, stream, order);
 }
 
-int32_t solb200_attn_dense(const void* q, const int64_t* q_strides, const void* k, const int64_t* k_strides,
-                           const void* v, const int64_t* v_strides, void* out, int64_t batch, int64_t q_tokens,
-                           int64_t kv_tokens, int64_t heads, int64_t head_dim, float scale, void* workspace,
-                           int64_t workspace_bytes, void* stream) {
+// Dense attention on the BF16 kernel (every key block exact); `bp` adds a mask (null: none).
+static int32_t attn_dense_impl(const void* q, const int64_t* q_strides, const void* k, const int64_t* k_strides,
+                               const void* v, const int64_t* v_strides, void* out, int64_t batch,
+                               int64_t q_tokens, int64_t kv_tokens, int64_t heads, int64_t head_dim, float scale,
+                               void* workspace, int64_t workspace_bytes, void* stream, const BiasParams* bp) {
   int32_t rc = check_device();
   if (rc) return rc;
   if (batch < 1 || q_tokens < 1 || kv_tokens < 1 || heads < 1)
@@ -526,11 +527,49 @@ int32_t solb200_attn_dense(const void* q, const int64_t* q_strides, const void* 
   m.kc = m.k;   // no pooled keys / values in a dense call: valid maps that are never loaded
   m.vc = m.v;
   {
-    NvtxRange r("solb200.dense");
-    e = launch_fwd_bf16((int)head_dim, BLK, m, fp, st);
+    NvtxRange r(bp ? "solb200.dense_masked" : "solb200.dense");
+    e = bp ? launch_fwd_bf16_masked((int)head_dim, m, fp, *bp, st) : launch_fwd_bf16((int)head_dim, BLK, m, fp, st);
   }
   if (e != cudaSuccess) return cuda_fail(e, "dense forward launch");
   return SOLB200_OK;
+}
+
+int32_t solb200_attn_dense(const void* q, const int64_t* q_strides, const void* k, const int64_t* k_strides,
+                           const void* v, const int64_t* v_strides, void* out, int64_t batch, int64_t q_tokens,
+                           int64_t kv_tokens, int64_t heads, int64_t head_dim, float scale, void* workspace,
+                           int64_t workspace_bytes, void* stream) {
+  return attn_dense_impl(q, q_strides, k, k_strides, v, v_strides, out, batch, q_tokens, kv_tokens, heads,
+                         head_dim, scale, workspace, workspace_bytes, stream, nullptr);
+}
+
+int32_t solb200_attn_dense_masked(const void* q, const int64_t* q_strides, const void* k,
+                                  const int64_t* k_strides, const void* v, const int64_t* v_strides,
+                                  const void* mask, int32_t mask_kind, const int64_t* mask_strides, void* out,
+                                  int64_t batch, int64_t q_tokens, int64_t kv_tokens, int64_t heads,
+                                  int64_t head_dim, float scale, void* workspace, int64_t workspace_bytes,
+                                  void* stream) {
+  if (!mask || !mask_strides) return fail(SOLB200_ERR_INVALID, "mask: null pointer or strides");
+  size_t esize = 0;
+  switch (mask_kind) {
+    case SOLB200_MASK_BOOL: esize = 1; break;
+    case SOLB200_MASK_F32: esize = 4; break;
+    case SOLB200_MASK_BF16:
+    case SOLB200_MASK_F16: esize = 2; break;
+    default: return fail(SOLB200_ERR_INVALID, "mask_kind must be SOLB200_MASK_BOOL, _F32, _BF16 or _F16");
+  }
+  if (reinterpret_cast<uintptr_t>(mask) % esize)
+    return fail(SOLB200_ERR_ALIGNMENT, "mask: not aligned to its element size");
+  BiasParams bp{};
+  bp.bias = mask;
+  bp.bias_kind = mask_kind;
+  bp.bias_mul = scale > 0.f ? 1.f / scale : 0.f;
+  for (int i = 0; i < 4; ++i) {
+    if (mask_strides[i] < 0 || mask_strides[i] > ((int64_t)1 << 40))
+      return fail(SOLB200_ERR_INVALID, "mask strides must be in [0, 2^40] elements (0 broadcasts)");
+    bp.bias_s[i] = mask_strides[i];
+  }
+  return attn_dense_impl(q, q_strides, k, k_strides, v, v_strides, out, batch, q_tokens, kv_tokens, heads,
+                         head_dim, scale, workspace, workspace_bytes, stream, &bp);
 }
 
 int32_t solb200_debug_set_wait(int64_t wait_ns, int32_t stall_unit) {

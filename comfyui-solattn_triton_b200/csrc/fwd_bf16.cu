@@ -26,12 +26,13 @@
 
 namespace solb200 {
 
-template <int HD, int BLK>
+// BIAS: the masked dense instantiation (a mask added to the exact scores, see add_bias_row).
+template <int HD, int BLK, bool BIAS>
 __global__ void __launch_bounds__(192, 2)
 sol_fwd_bf16_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
                     const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_kc,
                     const __grid_constant__ CUtensorMap tm_vc, const __grid_constant__ CUtensorMap tm_o,
-                    const FwdParams p) {
+                    const FwdParams p, const BiasParams bp) {
   pdl_begin();
   static_assert(HD == 64 || HD == 128, "head_dim 64 or 128");
   static_assert(BLK == 64 || BLK == 128, "block 64 or 128");
@@ -187,9 +188,15 @@ sol_fwd_bf16_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_const
     const int row = threadIdx.x;                       // 0..127 = TMEM lane
     const uint32_t lane_base = (uint32_t)(warp * 32) << 16;
     if (p.perm) prefetch_row_token<BLK>(p, u, row, sTok);
+    int64_t bias_off = -1;   // masked dense calls: this row's mask offset (row < BLK and q < T)
+    if constexpr (BIAS) {
+      const int64_t qtok = (int64_t)u.qb * BLK + row;
+      if (row < BLK && qtok < p.T) bias_off = u.b * bp.bias_s[0] + u.h * bp.bias_s[1] + qtok * bp.bias_s[2];
+    }
     float m_ref = -INFINITY, l_sum = 0.f;
     HalfIter<BLK> it(p, u);
     int s = 0, kind, row0;
+    auto bias = [&](uint32_t (&ra)[32], uint32_t (&rb)[32]) { add_bias_row(p, bp, bias_off, row0, ra, rb); };
     bool ok = true;
     for (; it.next(kind, row0); ++s) {
       const int slot = s & 1;
@@ -210,11 +217,19 @@ sol_fwd_bf16_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_const
       } else if (row0 + 64 > p.Tk) {
         colmask[0] = low_bits(p.Tk - row0);
         colmask[1] = low_bits(p.Tk - row0 - 32);
-        softmax_half<true, false, HD>(ts, tO + lane_base, colmask, p.s2, m_ref, l_sum, s > 0, -1, 0.f, 1.f,
-                                      drain);
+        if constexpr (BIAS)
+          softmax_half_pre<true, false, HD>(ts, tO + lane_base, colmask, p.s2, m_ref, l_sum, s > 0, -1, 0.f, 1.f,
+                                            drain, bias);
+        else
+          softmax_half<true, false, HD>(ts, tO + lane_base, colmask, p.s2, m_ref, l_sum, s > 0, -1, 0.f, 1.f,
+                                        drain);
       } else {
-        softmax_half<false, false, HD>(ts, tO + lane_base, colmask, p.s2, m_ref, l_sum, s > 0, -1, 0.f, 1.f,
-                                       drain);
+        if constexpr (BIAS)
+          softmax_half_pre<false, false, HD>(ts, tO + lane_base, colmask, p.s2, m_ref, l_sum, s > 0, -1, 0.f,
+                                             1.f, drain, bias);
+        else
+          softmax_half<false, false, HD>(ts, tO + lane_base, colmask, p.s2, m_ref, l_sum, s > 0, -1, 0.f, 1.f,
+                                         drain);
       }
       if (!ok) break;
       tmem_wait_st();
@@ -268,16 +283,16 @@ sol_fwd_bf16_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_const
 // q + K and V slots, barriers (256 B) and the output-token row (1 KB), plus 1 KB to align
 size_t fwd_bf16_smem_bytes(int hd) { return (size_t)(hd / 64) * (128 * 128 + 4 * 64 * 128) + 1024 + 256 + 1024; }
 
-template <int HD, int BLK>
-static cudaError_t launch_t(const FwdMaps& m, const FwdParams& p, cudaStream_t st) {
-  auto kern = sol_fwd_bf16_kernel<HD, BLK>;
+template <int HD, int BLK, bool BIAS = false>
+static cudaError_t launch_t(const FwdMaps& m, const FwdParams& p, cudaStream_t st, const BiasParams& bp = {}) {
+  auto kern = sol_fwd_bf16_kernel<HD, BLK, BIAS>;
   // at least ~100 KB so that at most two CTAs (512 TMEM columns) share an SM
   size_t smem = fwd_bf16_smem_bytes(HD);
   if (smem < 100 * 1024) smem = 100 * 1024;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return e;
   const unsigned grid = (unsigned)((int64_t)p.B * p.H * p.N);
-  return launch_pdl(kern, dim3(grid), dim3(192), smem, st, m.q, m.k, m.v, m.kc, m.vc, m.o, p);
+  return launch_pdl(kern, dim3(grid), dim3(192), smem, st, m.q, m.k, m.v, m.kc, m.vc, m.o, p, bp);
 }
 
 cudaError_t launch_fwd_bf16(int hd, int blk, const FwdMaps& m, const FwdParams& p, cudaStream_t st) {
@@ -285,6 +300,13 @@ cudaError_t launch_fwd_bf16(int hd, int blk, const FwdMaps& m, const FwdParams& 
   if (hd == 128 && blk == 64) return launch_t<128, 64>(m, p, st);
   if (hd == 64 && blk == 128) return launch_t<64, 128>(m, p, st);
   return launch_t<64, 64>(m, p, st);
+}
+
+// Masked dense calls: 128-token query tiles, every key block exact (p.mask null).
+cudaError_t launch_fwd_bf16_masked(int hd, const FwdMaps& m, const FwdParams& p, const BiasParams& bp,
+                                   cudaStream_t st) {
+  if (p.mask || !bp.bias) return cudaErrorInvalidValue;
+  return hd == 128 ? launch_t<128, 128, true>(m, p, st, bp) : launch_t<64, 128, true>(m, p, st, bp);
 }
 
 }  // namespace solb200

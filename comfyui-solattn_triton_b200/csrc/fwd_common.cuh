@@ -1,6 +1,7 @@
 // Pieces shared by the BF16 and INT8 block-sparse forward kernels.
 #pragma once
 
+#include <cuda_fp16.h>
 #include "common.cuh"
 
 namespace solb200 {
@@ -28,6 +29,20 @@ struct FwdParams {
   const int64_t* perm;
   __nv_bfloat16* out;
 };
+
+// Masked dense calls (BF16 kernel, its bias instantiation only): an attention mask read as
+// bias[b * bias_s[0] + h * bias_s[1] + q * bias_s[2] + k * bias_s[3]] (element strides, 0
+// broadcasts) of kind kBias*: a bool false masks the key, a float value is added to the
+// scaled score. bias_mul = 1 / scale, since the kernel adds the mask to the unscaled q . k.
+// A kernel parameter of its own: growing FwdParams changes the other kernels' registers.
+struct BiasParams {
+  const void* bias;
+  int bias_kind;
+  float bias_mul;
+  int64_t bias_s[4];
+};
+
+enum { kBiasNone = 0, kBiasBool = 1, kBiasF32 = 2, kBiasBF16 = 3, kBiasF16 = 4 };
 
 struct FwdMaps {
   CUtensorMap q, k, v, kc, vc, o;      // bf16 operands and output
@@ -302,14 +317,17 @@ __device__ __forceinline__ void softmax_tile(uint32_t t_s, uint32_t t_o, const u
 // One 64-column half of the online softmax for this thread's row. Same contract as
 // softmax_tile, plus `before_rescale`, called (warp-uniformly) before the accumulator
 // rows are rescaled so the caller can wait for in-flight P*V products first.
-template <bool MASKED, bool WEIGHTED, int HD, typename Hook>
-__device__ __forceinline__ void softmax_half(uint32_t t_s, uint32_t t_o, const uint32_t (&colmask)[2], float s2,
-                                             float& m_ref, float& l_sum, bool o_live, int tail_col,
-                                             float w_tail, float w_full, Hook&& before_rescale) {
+// `pre(ra, rb)` sees the half's raw scores (fp32 bits, columns 0-31 and 32-63) before
+// the column mask and the row max; softmax_half passes none.
+template <bool MASKED, bool WEIGHTED, int HD, typename Hook, typename Pre>
+__device__ __forceinline__ void softmax_half_pre(uint32_t t_s, uint32_t t_o, const uint32_t (&colmask)[2],
+                                                 float s2, float& m_ref, float& l_sum, bool o_live, int tail_col,
+                                                 float w_tail, float w_full, Hook&& before_rescale, Pre&& pre) {
   uint32_t ra[32], rb[32];
   tmem_ld32(t_s, ra);
   tmem_ld32(t_s + 32, rb);
   tmem_wait_ld();
+  pre(ra, rb);
   if (MASKED) {
 #pragma unroll
     for (int i = 0; i < 32; ++i) {
@@ -370,7 +388,45 @@ __device__ __forceinline__ void softmax_half(uint32_t t_s, uint32_t t_o, const u
   tmem_st16(t_s + 16, pb);
 }
 
+template <bool MASKED, bool WEIGHTED, int HD, typename Hook>
+__device__ __forceinline__ void softmax_half(uint32_t t_s, uint32_t t_o, const uint32_t (&colmask)[2], float s2,
+                                             float& m_ref, float& l_sum, bool o_live, int tail_col,
+                                             float w_tail, float w_full, Hook&& before_rescale) {
+  softmax_half_pre<MASKED, WEIGHTED, HD>(t_s, t_o, colmask, s2, m_ref, l_sum, o_live, tail_col, w_tail, w_full,
+                                         before_rescale, [](uint32_t (&)[32], uint32_t (&)[32]) {});
+}
+
+// Masked dense calls: adds this thread's mask row over keys k0 .. k0+63 to the raw scores
+// (a bool false, or a -inf value, makes the score -inf; keys >= Tk are left alone, the
+// column mask drops them). `row_off` is the element offset of mask[b, h, q, 0], or -1 for
+// a row past Tq (nothing is read).
+__device__ __forceinline__ float bias_value(const void* base, int kind, int64_t off) {
+  switch (kind) {
+    case kBiasBool: return __ldg(static_cast<const uint8_t*>(base) + off) ? 0.f : -INFINITY;
+    case kBiasF32: return __ldg(static_cast<const float*>(base) + off);
+    case kBiasBF16: return __bfloat162float(__ldg(static_cast<const __nv_bfloat16*>(base) + off));
+    default: return __half2float(__ldg(static_cast<const __half*>(base) + off));
+  }
+}
+
+__device__ __forceinline__ void add_bias_row(const FwdParams& p, const BiasParams& bp, int64_t row_off, int k0, uint32_t (&ra)[32],
+                                             uint32_t (&rb)[32]) {
+  if (row_off < 0) return;
+  const int n = min(64, p.Tk - k0);
+  const int64_t sk = bp.bias_s[3];
+#pragma unroll
+  for (int j = 0; j < 64; ++j) {
+    if (j < n) {
+      const float b = bias_value(bp.bias, bp.bias_kind, row_off + (int64_t)(k0 + j) * sk);
+      uint32_t& r = j < 32 ? ra[j & 31] : rb[j & 31];
+      r = __float_as_uint(b == -INFINITY ? -INFINITY : fmaf(b, bp.bias_mul, __uint_as_float(r)));
+    }
+  }
+}
+
 cudaError_t launch_fwd_bf16(int hd, int blk, const FwdMaps& m, const FwdParams& p, cudaStream_t st);
+cudaError_t launch_fwd_bf16_masked(int hd, const FwdMaps& m, const FwdParams& p, const BiasParams& bp,
+                                   cudaStream_t st);
 cudaError_t launch_fwd_int8(int hd, int blk, const FwdMaps& m, const FwdParams& p, cudaStream_t st);
 size_t fwd_bf16_smem_bytes(int hd);
 

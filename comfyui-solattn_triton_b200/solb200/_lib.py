@@ -55,6 +55,10 @@ _SIGS = {
     "solb200_attn_dense": (c_int32, [c_void_p, POINTER(c_int64), c_void_p, POINTER(c_int64), c_void_p,
                                      POINTER(c_int64), c_void_p, c_int64, c_int64, c_int64, c_int64, c_int64,
                                      c_float, c_void_p, c_int64, c_void_p]),
+    "solb200_attn_dense_masked": (c_int32, [c_void_p, POINTER(c_int64), c_void_p, POINTER(c_int64), c_void_p,
+                                            POINTER(c_int64), c_void_p, c_int32, POINTER(c_int64), c_void_p,
+                                            c_int64, c_int64, c_int64, c_int64, c_int64, c_float, c_void_p,
+                                            c_int64, c_void_p]),
     "solb200_workspace_bytes_reordered": (c_int32, [c_int64, c_int64, c_int64, c_int64, c_int32, c_int32,
                                                     c_int32, POINTER(c_int64)]),
     "solb200_sol_attn_reordered": (c_int32, [c_void_p, POINTER(c_int64), c_void_p, POINTER(c_int64), c_void_p,

@@ -195,12 +195,45 @@ def sol_attn_int8(q, k, v, *, scale=None, tau=1.0, sink_blocks=(0, 0), sink_q=(0
     return out
 
 
-def dense_attn(q, k, v, *, scale=None):
-    """Dense BF16 attention softmax(q k^T * scale) v on the sm_100a tensor cores (C ABI
-    ``solb200_attn_dense``): q [B, Tq, H, D], k / v [B, Tk, H, D] (BTHD, any strides with a
-    contiguous head dim; Tq may differ from Tk), D 64 or 128; returns a fresh [B, Tq, H, D]
-    bf16 tensor. For the calls the Sol-Attn path declines (cross-attention, head_dim != 128,
-    short sequences), which the reference hands back to the host's attention."""
+# element types of an attention mask, as the C ABI numbers them (SOLB200_MASK_*)
+MASK_KINDS = {torch.bool: 1, torch.float32: 2, torch.bfloat16: 3, torch.float16: 4}
+
+
+def mask_layout(mask, B, H, Tq, Tk):
+    """(mask, kind, [4 element strides]) of an attention mask for queries [B, Tq, H, D] and
+    keys [B, Tk, H, D], read the way the host's attention reads one: a 2-D mask is
+    [Tq, Tk], a 3-D mask [B, Tq, Tk] (every head alike), a 4-D mask [B, H, Tq, Tk]; a
+    dimension of size 1 broadcasts (stride 0). bool masks attend where true; float masks
+    are added to the scaled scores. Raises ValueError for any other shape or dtype."""
+    if mask.dtype not in MASK_KINDS:
+        raise ValueError(f"solb200: mask dtype {mask.dtype} is not bool, float32, bfloat16 or float16")
+    m = mask
+    if m.dim() == 2:
+        m = m.unsqueeze(0)
+    if m.dim() == 3:
+        m = m.unsqueeze(1)
+    if m.dim() != 4:
+        raise ValueError(f"solb200: mask of shape {tuple(mask.shape)} is not 2-, 3- or 4-D")
+    strides = []
+    for size, want, st in zip(m.shape, (B, H, Tq, Tk), m.stride()):
+        if size == 1:
+            strides.append(0)
+        elif size == want:
+            strides.append(st)
+        else:
+            raise ValueError(f"solb200: mask of shape {tuple(mask.shape)} does not broadcast to "
+                             f"{(B, H, Tq, Tk)}")
+    return m, MASK_KINDS[m.dtype], strides
+
+
+def dense_attn(q, k, v, *, scale=None, mask=None):
+    """Dense BF16 attention softmax(q k^T * scale + mask) v on the sm_100a tensor cores (C
+    ABI ``solb200_attn_dense`` / ``solb200_attn_dense_masked``): q [B, Tq, H, D], k / v
+    [B, Tk, H, D] (BTHD, any strides with a contiguous head dim; Tq may differ from Tk), D
+    64 or 128; ``mask`` as ``mask_layout`` reads it (None: no mask); returns a fresh
+    [B, Tq, H, D] bf16 tensor. For the calls the Sol-Attn path declines (cross-attention,
+    head_dim != 128, short sequences, masks), which the reference hands back to the host's
+    attention."""
     q, k, v = _ready(q, "q"), _ready(k, "k"), _ready(v, "v")
     if k.shape != v.shape or q.shape[0] != k.shape[0] or q.shape[2:] != k.shape[2:]:
         raise RuntimeError(f"solb200: dense_attn shapes q {tuple(q.shape)}, k {tuple(k.shape)}, "
@@ -210,12 +243,22 @@ def dense_attn(q, k, v, *, scale=None):
     B, Tq, H, D = q.shape
     Tk = k.shape[1]
     scale = D ** -0.5 if scale is None else float(scale)
+    if mask is not None:
+        if mask.device != q.device:
+            raise RuntimeError("solb200: mask on a different device from q")
+        m, kind, ms = mask_layout(mask, B, H, Tq, Tk)
     with torch.cuda.device(q.device):
         ws = torch.empty(256, dtype=torch.uint8, device=q.device)
         out = torch.empty((B, Tq, H, D), dtype=torch.bfloat16, device=q.device)
-        rc = lib().solb200_attn_dense(q.data_ptr(), _strides(q), k.data_ptr(), _strides(k), v.data_ptr(),
-                                      _strides(v), out.data_ptr(), B, Tq, Tk, H, D, scale, ws.data_ptr(), 256,
-                                      _stream_ptr(q.device))
+        if mask is None:
+            rc = lib().solb200_attn_dense(q.data_ptr(), _strides(q), k.data_ptr(), _strides(k), v.data_ptr(),
+                                          _strides(v), out.data_ptr(), B, Tq, Tk, H, D, scale, ws.data_ptr(), 256,
+                                          _stream_ptr(q.device))
+        else:
+            rc = lib().solb200_attn_dense_masked(q.data_ptr(), _strides(q), k.data_ptr(), _strides(k),
+                                                 v.data_ptr(), _strides(v), m.data_ptr(), kind,
+                                                 (c_int64 * 4)(*ms), out.data_ptr(), B, Tq, Tk, H, D, scale,
+                                                 ws.data_ptr(), 256, _stream_ptr(q.device))
         check(rc, "dense_attn")
         if _SYNC_CHECK:
             code = c_int32(0)

@@ -16,6 +16,10 @@ Reference behaviour this module reproduces (kijai/ComfyUI-SolAttn_triton):
     sol_attn_stats         __init__.py:144-152   dispatch counters
     attention_sol          __init__.py:649-663   registry entry with defaults
 
+This build's additions: declined calls that the dense sm_100a kernel can take run there
+(``_run``'s dense branch, counter ``dense_b200``), and so do masked calls (``_run_masked``,
+counter ``masked_b200``), which the reference always hands to the host.
+
 Nothing here imports ComfyUI: ``func`` (the host's dense attention) is passed in by
 the caller, as the host does. The ComfyUI node classes live in the package's
 top-level ``__init__.py``.
@@ -35,7 +39,7 @@ HEAD_DIM = 128
 BLOCK_SIZE = 64          # routing block of the override (the reference's constant)
 
 _stats = {"sparse": 0, "dense_fallback": 0, "outside_range": 0, "dense_block": 0, "errors": 0,
-          "dense_b200": 0}
+          "dense_b200": 0, "masked_b200": 0}
 _seen = set()
 _probe = {}
 
@@ -179,6 +183,33 @@ def _run(q, k, v, heads, skip_reshape, skip_output_reshape, scale, tau, min_toke
     return out.reshape(b, -1, heads * dim_head)
 
 
+def _run_masked(q, k, v, heads, mask, skip_reshape, skip_output_reshape, scale, verbose):
+    """A masked call on the dense B200 kernel (``ops.dense_attn`` with the mask), in the
+    caller's layout, or None when the host must take it: the reference declines every
+    masked call (``__init__.py:170-189``); this build runs the ones whose tensors the dense
+    kernel takes and whose mask ``ops.mask_layout`` reads (bool or float, broadcastable
+    to [B, H, Tq, Tk])."""
+    if skip_reshape:                         # BHND
+        b, _, _, dim_head = q.shape
+        qs, ks, vs = (t.transpose(1, 2) for t in (q, k, v))
+    else:                                    # B, N, heads*dim_head
+        b, _, width = q.shape
+        dim_head = width // heads
+        qs, ks, vs = (t.view(b, -1, heads, dim_head) for t in (q, k, v))
+    if not _dense_capable(qs, ks, vs, dim_head) or mask.device != q.device:
+        return None
+    try:
+        ops.mask_layout(mask, qs.shape[0], heads, qs.shape[1], ks.shape[1])
+    except ValueError:
+        return None
+    out = ops.dense_attn(qs, ks, vs, scale=scale, mask=mask)
+    _stats["masked_b200"] += 1
+    if verbose:
+        _log_once((tuple(qs.shape), tuple(mask.shape), "masked"),
+                  f"masked dense sm_100a {tuple(qs.shape)} mask {tuple(mask.shape)} {mask.dtype}")
+    return out.transpose(1, 2) if skip_output_reshape else out.reshape(b, -1, heads * dim_head)
+
+
 def _sink_blocks(transformer_options, tokens, mode, block=BLOCK_SIZE):
     """(exact-KV block range, dense-query block range) for MiniMax-H3's packed
     conditioning rows [text][cond][ref][audio][video]: every block up to the one holding
@@ -211,8 +242,17 @@ def make_override(tau=1.0, min_tokens=4096, sigma_start=None, sigma_end=None, ve
                           **kwargs)
 
         if mask is not None:
-            _stats["dense_fallback"] += 1
-            return dense()
+            try:
+                out = _run_masked(q, k, v, heads, mask, skip_reshape, skip_output_reshape,
+                                  kwargs.get("scale", None), verbose)
+            except Exception as exc:
+                _stats["errors"] += 1
+                _log_kernel_failure(exc)
+                out = None
+            if out is None:
+                _stats["dense_fallback"] += 1
+                return dense()
+            return out
         options = kwargs.get("transformer_options", {}) or {}
         depth = options.get("sol_block") if (dense_blocks or tau_profile) else None
         if depth in dense_blocks:
@@ -291,15 +331,18 @@ def attention_sol(q, k, v, heads, mask=None, attn_precision=None, skip_reshape=F
                   skip_output_reshape=False, dense=None, **kwargs):
     """Registry entry point with the defaults (tau 1.0, min_tokens 4096, no gates);
     ``dense`` is the host's fallback attention."""
-    if mask is None:
-        try:
+    try:
+        if mask is None:
             out = _run(q, k, v, heads, skip_reshape, skip_output_reshape, kwargs.get("scale", None),
                        1.0, 4096, False)
-            if out is not None:
-                return out
-        except Exception as exc:
-            _stats["errors"] += 1
-            _log_kernel_failure(exc)
+        else:
+            out = _run_masked(q, k, v, heads, mask, skip_reshape, skip_output_reshape,
+                              kwargs.get("scale", None), False)
+        if out is not None:
+            return out
+    except Exception as exc:
+        _stats["errors"] += 1
+        _log_kernel_failure(exc)
     if dense is None:
         raise RuntimeError("solb200.attention_sol: no dense fallback given for a declined call")
     return dense(q, k, v, heads, mask=mask, skip_reshape=skip_reshape,

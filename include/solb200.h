@@ -172,6 +172,30 @@ SOLB200_API int32_t solb200_attn_dense(const void* q, const int64_t* q_strides, 
                                        int64_t heads, int64_t head_dim, float scale, void* workspace,
                                        int64_t workspace_bytes, void* stream);
 
+/* Element types of the mask of solb200_attn_dense_masked. */
+enum {
+  SOLB200_MASK_BOOL = 1,  /* one byte per element: nonzero attends, zero masks the key */
+  SOLB200_MASK_F32 = 2,   /* float added to the scaled score (-inf masks the key) */
+  SOLB200_MASK_BF16 = 3,
+  SOLB200_MASK_F16 = 4
+};
+
+/* solb200_attn_dense with an attention mask, as the host's scaled_dot_product_attention
+ * applies one: out = softmax(q k^T * scale + M) v. A bool mask puts -inf where it is false;
+ * a float mask is added. The mask element for (batch b, head h, query token i, key token j)
+ * is mask[b * s[0] + h * s[1] + i * s[2] + j * s[3]], s = mask_strides in elements. A stride
+ * of 0 broadcasts that dimension, so [1, 1, 1, kv_tokens] key-padding masks and
+ * [q_tokens, kv_tokens] masks are passed without a copy. The caller guarantees that every
+ * such element lies inside the mask's allocation. A query row whose keys are all masked comes
+ * out NaN (0 / 0). The override routes masked calls here; the reference declines every
+ * masked call to the host's attention (__init__.py:170-189). */
+SOLB200_API int32_t solb200_attn_dense_masked(const void* q, const int64_t* q_strides, const void* k,
+                                              const int64_t* k_strides, const void* v, const int64_t* v_strides,
+                                              const void* mask, int32_t mask_kind, const int64_t* mask_strides,
+                                              void* out, int64_t batch, int64_t q_tokens, int64_t kv_tokens,
+                                              int64_t heads, int64_t head_dim, float scale, void* workspace,
+                                              int64_t workspace_bytes, void* stream);
+
 /* BF16 Sol-Attn that allocates nothing, for hosts that cannot hand this library device
  * memory at call time (an application that plans all device allocations up front and
  * forbids allocating later, a plugin whose host owns the allocator, or a caller that

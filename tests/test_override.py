@@ -209,3 +209,35 @@ def test_node_module_with_stub_comfy(monkeypatch):
         "optimized_attention_override"])
     with pytest.raises(RuntimeError):
         mod.SolAttnBlockProbe.execute(model)     # no override to measure
+
+
+def test_mask_layout_reads_masks_like_the_host():
+    """``ops.mask_layout``: the host's 2-D / 3-D / 4-D mask conventions as element strides over
+    [B, H, Tq, Tk], size-1 dimensions broadcast (stride 0); other shapes and dtypes refused."""
+    from solb200 import ops
+    B, H, Tq, Tk = 2, 3, 5, 7
+    _, kind, st = ops.mask_layout(torch.zeros(Tq, Tk), B, H, Tq, Tk)
+    assert (kind, st) == (2, [0, 0, Tk, 1])
+    _, kind, st = ops.mask_layout(torch.zeros(B, Tq, Tk, dtype=torch.float16), B, H, Tq, Tk)
+    assert (kind, st) == (4, [Tq * Tk, 0, Tk, 1])
+    _, kind, st = ops.mask_layout(torch.zeros(B, 1, 1, Tk, dtype=torch.bool), B, H, Tq, Tk)
+    assert (kind, st) == (1, [0 if B == 1 else Tk, 0, 0, 1])
+    _, kind, st = ops.mask_layout(torch.zeros(1, H, Tq, Tk, dtype=torch.bfloat16), B, H, Tq, Tk)
+    assert (kind, st) == (3, [0, Tq * Tk, Tk, 1])
+    _, _, st = ops.mask_layout(torch.zeros(1, 1, 1, Tk).expand(B, H, Tq, Tk), B, H, Tq, Tk)
+    assert st == [0, 0, 0, 1]
+    _, _, st = ops.mask_layout(torch.zeros(Tk, Tq).t(), B, H, Tq, Tk)     # a transposed view
+    assert st == [0, 0, 1, Tq]
+    for bad in (torch.zeros(Tq, Tk, dtype=torch.int64), torch.zeros(Tq, Tk, dtype=torch.float64),
+                torch.zeros(B * H, Tq, Tk), torch.zeros(Tq + 1, Tk), torch.zeros(Tk),
+                torch.zeros(1, 1, 1, 1, Tk)):
+        with pytest.raises(ValueError):
+            ops.mask_layout(bad, B, H, Tq, Tk)
+
+
+def test_masked_call_on_cpu_goes_to_the_host():
+    ov.reset_sol_attn_stats()
+    dense = Dense()
+    q, k, v = _qkv()
+    ov.make_override(tau=1.0, min_tokens=0)(dense, q, k, v, 2, mask=torch.zeros(64, 64))
+    assert ov.sol_attn_stats()["dense_fallback"] == 1 and ov.sol_attn_stats()["masked_b200"] == 0
