@@ -730,6 +730,61 @@ def triton_bar(args):
     emit({"triton_reference": res})
 
 
+def h2d_probe(args):
+    """The host link the e2e leg runs against: copy-engine rates for one config-3 tensor
+    (40 heads x 32760 tokens x 128, bf16, 335 MB) between pinned host memory and the GPU,
+    as one 1-D copy and as the head-chunk 2-D copies ``solb200_copy_heads`` issues for
+    ``sol_attn_host`` (1, 2, 5 and 40 heads per row), each direction alone and the 2-head
+    rows both ways at once (the e2e leg's overlap). One line, then exit."""
+    import torch
+    from solb200._lib import check, lib
+    from solb200.workloads import CONFIGS
+    cfg = CONFIGS["c3"]
+    B, T, H, D = cfg.batch, cfg.tokens, cfg.heads, cfg.head_dim
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    host_in = torch.randn(B, T, H, D).to(torch.bfloat16).pin_memory()
+    host_out = torch.empty_like(host_in).pin_memory()
+    dbuf = torch.empty(B, T, H, D, dtype=torch.bfloat16, device=dev)
+    dbuf2 = torch.empty_like(dbuf)
+    nbytes = host_in.numel() * host_in.element_size()
+    s_in, s_out = torch.cuda.Stream(dev), torch.cuda.Stream(dev)
+    L = lib()
+
+    def chunks(hc, to_device, stream, dst_dev):
+        for h0 in range(0, H, hc):
+            n = min(hc, H - h0)
+            d = dst_dev.data_ptr() + h0 * B * T * D * 2     # chunk slots back to back
+            h = (host_in if to_device else host_out).data_ptr()
+            check(L.solb200_copy_heads(d, h, B, T, H, D, h0, n, int(to_device), stream.cuda_stream), "copy_heads")
+
+    def rate(fn, streams, moved):
+        fn()
+        torch.cuda.synchronize()
+        best = float("inf")
+        for _ in range(max(3, args.steps)):
+            t0 = [torch.cuda.Event(enable_timing=True) for _ in streams]
+            t1 = [torch.cuda.Event(enable_timing=True) for _ in streams]
+            for s, e in zip(streams, t0):
+                e.record(s)
+            fn()
+            for s, e in zip(streams, t1):
+                e.record(s)
+            torch.cuda.synchronize()
+            best = min(best, max(a.elapsed_time(b) for a, b in zip(t0, t1)))
+        return {"ms": best, "gbs": moved / (best * 1e-3) / 1e9}
+
+    res = {"tensor_bytes": nbytes, "workload": "config3_video480p_B1_H40_T32760_D128 (one of q/k/v/out)"}
+    res["h2d_1d"] = rate(lambda: dbuf.copy_(host_in, non_blocking=True), [torch.cuda.current_stream(dev)], nbytes)
+    res["d2h_1d"] = rate(lambda: host_out.copy_(dbuf, non_blocking=True), [torch.cuda.current_stream(dev)], nbytes)
+    for hc in (1, 2, 5, 40):
+        res[f"h2d_{hc}head_rows"] = rate(lambda: chunks(hc, True, s_in, dbuf), [s_in], nbytes)
+    res["d2h_2head_rows"] = rate(lambda: chunks(2, False, s_out, dbuf2), [s_out], nbytes)
+    both = rate(lambda: (chunks(2, True, s_in, dbuf), chunks(2, False, s_out, dbuf2)), [s_in, s_out], 2 * nbytes)
+    res["both_ways_2head_rows"] = {"ms": both["ms"], "gbs_each_way": both["gbs"] / 2}
+    emit({"h2d_probe": res})
+
+
 def main():
     _isolate_stdout()
     ap = argparse.ArgumentParser()
@@ -753,8 +808,13 @@ def main():
                     help="profiling only: run this many of the 40 heads (0 = all)")
     ap.add_argument("--triton-bar", action="store_true",
                     help="time the reference's Triton kernels on this GPU (one line, then exit)")
+    ap.add_argument("--h2d-probe", action="store_true",
+                    help="time the host link the e2e leg uses (one line, then exit)")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
+    if args.h2d_probe:
+        h2d_probe(args)
+        return
     if args.triton_bar:
         triton_bar(args)
         return
