@@ -26,8 +26,9 @@
 
 namespace solb200 {
 
-// BIAS: the masked dense instantiation (a mask added to the exact scores, see add_bias_row).
-template <int HD, int BLK, bool BIAS>
+// BIAS: 0, or the mask kind (kBias*) of a masked dense instantiation (a mask added to the
+// exact scores, see add_bias_row).
+template <int HD, int BLK, int BIAS>
 __global__ void __launch_bounds__(192, 2)
 sol_fwd_bf16_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
                     const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_kc,
@@ -196,7 +197,9 @@ sol_fwd_bf16_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_const
     float m_ref = -INFINITY, l_sum = 0.f;
     HalfIter<BLK> it(p, u);
     int s = 0, kind, row0;
-    auto bias = [&](uint32_t (&ra)[32], uint32_t (&rb)[32]) { add_bias_row(p, bp, bias_off, row0, ra, rb); };
+    auto bias = [&](uint32_t (&ra)[32], uint32_t (&rb)[32]) {
+      add_bias_row<BIAS == 0 ? kBiasF32 : BIAS>(p, bp, bias_off, row0, ra, rb);
+    };
     bool ok = true;
     for (; it.next(kind, row0); ++s) {
       const int slot = s & 1;
@@ -283,7 +286,7 @@ sol_fwd_bf16_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_const
 // q + K and V slots, barriers (256 B) and the output-token row (1 KB), plus 1 KB to align
 size_t fwd_bf16_smem_bytes(int hd) { return (size_t)(hd / 64) * (128 * 128 + 4 * 64 * 128) + 1024 + 256 + 1024; }
 
-template <int HD, int BLK, bool BIAS = false>
+template <int HD, int BLK, int BIAS = 0>
 static cudaError_t launch_t(const FwdMaps& m, const FwdParams& p, cudaStream_t st, const BiasParams& bp = {}) {
   auto kern = sol_fwd_bf16_kernel<HD, BLK, BIAS>;
   // at least ~100 KB so that at most two CTAs (512 TMEM columns) share an SM
@@ -306,7 +309,18 @@ cudaError_t launch_fwd_bf16(int hd, int blk, const FwdMaps& m, const FwdParams& 
 cudaError_t launch_fwd_bf16_masked(int hd, const FwdMaps& m, const FwdParams& p, const BiasParams& bp,
                                    cudaStream_t st) {
   if (p.mask || !bp.bias) return cudaErrorInvalidValue;
-  return hd == 128 ? launch_t<128, 128, true>(m, p, st, bp) : launch_t<64, 128, true>(m, p, st, bp);
+  switch (bp.bias_kind) {
+    case kBiasBool:
+      return hd == 128 ? launch_t<128, 128, kBiasBool>(m, p, st, bp) : launch_t<64, 128, kBiasBool>(m, p, st, bp);
+    case kBiasF32:
+      return hd == 128 ? launch_t<128, 128, kBiasF32>(m, p, st, bp) : launch_t<64, 128, kBiasF32>(m, p, st, bp);
+    case kBiasBF16:
+      return hd == 128 ? launch_t<128, 128, kBiasBF16>(m, p, st, bp) : launch_t<64, 128, kBiasBF16>(m, p, st, bp);
+    case kBiasF16:
+      return hd == 128 ? launch_t<128, 128, kBiasF16>(m, p, st, bp) : launch_t<64, 128, kBiasF16>(m, p, st, bp);
+    default:
+      return cudaErrorInvalidValue;
+  }
 }
 
 }  // namespace solb200

@@ -400,27 +400,59 @@ __device__ __forceinline__ void softmax_half(uint32_t t_s, uint32_t t_o, const u
 // (a bool false, or a -inf value, makes the score -inf; keys >= Tk are left alone, the
 // column mask drops them). `row_off` is the element offset of mask[b, h, q, 0], or -1 for
 // a row past Tq (nothing is read).
-__device__ __forceinline__ float bias_value(const void* base, int kind, int64_t off) {
-  switch (kind) {
-    case kBiasBool: return __ldg(static_cast<const uint8_t*>(base) + off) ? 0.f : -INFINITY;
-    case kBiasF32: return __ldg(static_cast<const float*>(base) + off);
-    case kBiasBF16: return __bfloat162float(__ldg(static_cast<const __nv_bfloat16*>(base) + off));
-    default: return __half2float(__ldg(static_cast<const __half*>(base) + off));
-  }
+template <int KIND>
+__device__ __forceinline__ float bias_value(const void* base, int64_t off) {
+  if (KIND == kBiasBool) return __ldg(static_cast<const uint8_t*>(base) + off) ? 0.f : -INFINITY;
+  if (KIND == kBiasF32) return __ldg(static_cast<const float*>(base) + off);
+  if (KIND == kBiasBF16) return __bfloat162float(__ldg(static_cast<const __nv_bfloat16*>(base) + off));
+  return __half2float(__ldg(static_cast<const __half*>(base) + off));
 }
 
-__device__ __forceinline__ void add_bias_row(const FwdParams& p, const BiasParams& bp, int64_t row_off, int k0, uint32_t (&ra)[32],
-                                             uint32_t (&rb)[32]) {
+// element j of a 16-byte vector of mask elements, as the value added to a score
+template <int KIND>
+__device__ __forceinline__ float bias_lane(const uint4& w, int j) {
+  constexpr int ES = KIND == kBiasBool ? 1 : (KIND == kBiasF32 ? 4 : 2);
+  const int wi = (j * ES) >> 2;
+  const uint32_t word = wi == 0 ? w.x : (wi == 1 ? w.y : (wi == 2 ? w.z : w.w));
+  if (KIND == kBiasBool) return ((word >> ((j & 3) * 8)) & 0xffu) ? 0.f : -INFINITY;
+  if (KIND == kBiasF32) return __uint_as_float(word);
+  const uint16_t h = (uint16_t)(word >> ((j & 1) * 16));
+  if (KIND == kBiasBF16) return __uint_as_float((uint32_t)h << 16);
+  return __half2float(__ushort_as_half(h));
+}
+
+template <int KIND>
+__device__ __forceinline__ void add_bias_value(uint32_t& r, float b, float mul) {
+  r = __float_as_uint(b == -INFINITY ? -INFINITY : fmaf(b, mul, __uint_as_float(r)));
+}
+
+template <int KIND>
+__device__ __forceinline__ void add_bias_row(const FwdParams& p, const BiasParams& bp, int64_t row_off, int k0,
+                                             uint32_t (&ra)[32], uint32_t (&rb)[32]) {
   if (row_off < 0) return;
+  constexpr int ES = KIND == kBiasBool ? 1 : (KIND == kBiasF32 ? 4 : 2);   // bytes per element
+  constexpr int EPV = 16 / ES;                                              // elements per 16 bytes
   const int n = min(64, p.Tk - k0);
   const int64_t sk = bp.bias_s[3];
+  const uint8_t* base = static_cast<const uint8_t*>(bp.bias) + (row_off + (int64_t)k0 * sk) * ES;
+  if (n == 64 && sk == 1 && (reinterpret_cast<uintptr_t>(base) & 15u) == 0) {
+    // a contiguous, 16-byte-aligned row of 64 elements: 64 * ES / 16 vector loads
+#pragma unroll
+    for (int v = 0; v < 64 / EPV; ++v) {
+      const uint4 w = __ldg(reinterpret_cast<const uint4*>(base) + v);
+#pragma unroll
+      for (int j = 0; j < EPV; ++j) {
+        const int c = v * EPV + j;
+        add_bias_value<KIND>(c < 32 ? ra[c & 31] : rb[c & 31], bias_lane<KIND>(w, j), bp.bias_mul);
+      }
+    }
+    return;
+  }
 #pragma unroll
   for (int j = 0; j < 64; ++j) {
-    if (j < n) {
-      const float b = bias_value(bp.bias, bp.bias_kind, row_off + (int64_t)(k0 + j) * sk);
-      uint32_t& r = j < 32 ? ra[j & 31] : rb[j & 31];
-      r = __float_as_uint(b == -INFINITY ? -INFINITY : fmaf(b, bp.bias_mul, __uint_as_float(r)));
-    }
+    if (j < n)
+      add_bias_value<KIND>(j < 32 ? ra[j & 31] : rb[j & 31], bias_value<KIND>(base, (int64_t)j * sk),
+                           bp.bias_mul);
   }
 }
 
